@@ -1,0 +1,983 @@
+// C ABI of the B200 ESM-2 encoder forward: context, weight upload, workspace, and the per-layer
+// launch sequence that replaces codon-infer's forward_bidirectional* (src/lib.rs:5078-6147).
+//
+// Per layer (stream-ordered, no host synchronisation):
+//   dequantize the layer's six matrices to fp16 (L2-resident scratch)
+//   LN1 -> QKV GEMM (+bias, +RoPE) -> attention (-> contact accumulation) -> Wo GEMM (+bias, += x)
+//   LN2 -> fc1 GEMM (+bias, GELU) -> fc2 GEMM (+bias, += x)
+// then LN_f, the LM head (dense GEMM + GELU, LN + decoder) and, with contacts, the APC finalize.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/esm_b200.h"
+#include "common.cuh"
+#include "formats.h"
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+
+using esm::CodqHeader;
+
+struct esm_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  std::mutex mu;
+  std::string err;
+  int* d_err = nullptr;
+
+  // ---- weights ----
+  bool loaded = false;
+  esm_config cfg{};
+  int dtype = 0;
+  std::vector<void*> w_allocs;
+  void* w[ESM_NUM_TENSORS] = {};
+  int64_t classifier_floats = 0;
+  bool has_head = false;
+  float* bqkv = nullptr;         // [nl, 3d]
+  float* emb_f32 = nullptr;      // [V, d] fp32 embedding (dequantized copy for Q8 models)
+  __half* dense16 = nullptr;     // LM-head dense weight in fp16 [d, d]
+  __half* wqkv16 = nullptr;      // per-layer fp16 scratch
+  __half* wo16 = nullptr;
+  __half* w116 = nullptr;
+  __half* w216 = nullptr;
+  CUtensorMap tm_wqkv, tm_wo, tm_w1, tm_w2, tm_dense;
+  int bn_qkv = 0, bn_o = 0, bn_fc1 = 0, bn_fc2 = 0, bn_dense = 0;
+
+  // ---- contact head ----
+  bool has_ch = false;
+  float ch_b = 0.0f;
+  float* d_ch_w = nullptr;
+
+  // ---- workspace ----
+  int cap_tokens = 0, cap_seqs = 0, cap_len = 0;
+  bool cap_contacts = false;
+  int64_t cap_rows = 0, work_cap = 0, tiles_cap = 0, m_cap = 0, r_cap = 0;
+  std::vector<void*> ws_allocs;
+  float* x = nullptr;
+  __half* xn = nullptr;
+  __half* qkv = nullptr;
+  __half* ao = nullptr;
+  __half* hb = nullptr;
+  float* headf = nullptr;
+  float* hidden = nullptr;
+  float* logits = nullptr;
+  float* lse = nullptr;
+  float2* rope = nullptr;
+  int32_t* pos = nullptr;
+  int32_t* seq_of = nullptr;
+  int32_t* tokens = nullptr;
+  int32_t* cu = nullptr;
+  float* escale = nullptr;
+  int2* work = nullptr;
+  int4* ctiles = nullptr;
+  int64_t* m_off = nullptr;
+  int64_t* r_off = nullptr;
+  float* M = nullptr;
+  float* r = nullptr;
+  float* a_scr = nullptr;
+  float* cmap = nullptr;
+  CUtensorMap tm_xn, tm_ao, tm_hb;
+  // pinned staging of the per-call plan, and the event that says it may be rewritten
+  int32_t* h_cu = nullptr;
+  int2* h_work = nullptr;
+  int4* h_tiles = nullptr;
+  int64_t* h_moff = nullptr;
+  int64_t* h_roff = nullptr;
+  cudaEvent_t plan_ev = nullptr;
+  std::vector<int32_t> plan_key;
+  int plan_work = 0, plan_tiles = 0;
+  // host-API staging (grows on demand)
+  int32_t* d_padded_tokens = nullptr;
+  size_t padded_tok_cap = 0;
+  float* d_padded_out = nullptr;
+  size_t padded_out_cap = 0;
+};
+
+namespace {
+
+int fail(esm_ctx* c, int code, const std::string& msg) {
+  if (c) c->err = msg;
+  return code;
+}
+
+#define ESM_CUDA(call)                                                                          \
+  do {                                                                                          \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess)                                                                      \
+      return fail(c, e_ == cudaErrorMemoryAllocation ? ESM_ENOMEM : ESM_ECUDA,                  \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                          \
+  } while (0)
+
+template <typename T>
+int dev_alloc(esm_ctx* c, std::vector<void*>& list, T** out, size_t count) {
+  void* p = nullptr;
+  const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(c, ESM_ENOMEM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+  list.push_back(p);
+  *out = static_cast<T*>(p);
+  return ESM_OK;
+}
+
+void free_list(std::vector<void*>& list) {
+  for (void* p : list) cudaFree(p);
+  list.clear();
+}
+
+void free_pinned(esm_ctx* c) {
+  for (void* p : {static_cast<void*>(c->h_cu), static_cast<void*>(c->h_work), static_cast<void*>(c->h_tiles),
+                  static_cast<void*>(c->h_moff), static_cast<void*>(c->h_roff)})
+    if (p) cudaFreeHost(p);
+  c->h_cu = nullptr;
+  c->h_work = nullptr;
+  c->h_tiles = nullptr;
+  c->h_moff = nullptr;
+  c->h_roff = nullptr;
+}
+
+bool shape_supported(const esm_config& c, std::string* why) {
+  const int d = c.dim, H = c.n_heads;
+  if (d <= 0 || H <= 0 || c.hidden_dim <= 0 || c.n_layers <= 0 || c.vocab_size <= 0) {
+    *why = "non-positive dimension";
+    return false;
+  }
+  if (d % 32 || c.hidden_dim % 32) {
+    *why = "dim and hidden_dim must be multiples of 32 (Q-block size)";
+    return false;
+  }
+  if (d % H) {
+    *why = "dim must be divisible by n_heads";
+    return false;
+  }
+  const int dh = d / H;
+  if (dh != 16 && dh != 24 && dh != 32 && dh != 64) {
+    *why = "head_dim must be 16, 24, 32 or 64 (the ESM-2 family)";
+    return false;
+  }
+  if (d > 2560 || H > 64) {
+    *why = "dim above 2560 or more than 64 heads";
+    return false;
+  }
+  if (!esm::gemm_pick_bn(3 * d, dh) || !esm::gemm_pick_bn(d, 0) || !esm::gemm_pick_bn(c.hidden_dim, 0)) {
+    *why = "no GEMM tile width divides the projection sizes";
+    return false;
+  }
+  return true;
+}
+
+int build_weight_maps(esm_ctx* c) {
+  const int d = c->cfg.dim, F = c->cfg.hidden_dim, dh = d / c->cfg.n_heads;
+  c->bn_qkv = esm::gemm_pick_bn(3 * d, dh);
+  c->bn_o = esm::gemm_pick_bn(d, 0);
+  c->bn_fc1 = esm::gemm_pick_bn(F, 0);
+  c->bn_fc2 = esm::gemm_pick_bn(d, 0);
+  c->bn_dense = esm::gemm_pick_bn(d, 0);
+  bool ok = esm::make_tmap_f16(&c->tm_wqkv, c->wqkv16, 3 * d, d, d, c->bn_qkv) &&
+            esm::make_tmap_f16(&c->tm_wo, c->wo16, d, d, d, c->bn_o) &&
+            esm::make_tmap_f16(&c->tm_w1, c->w116, F, d, d, c->bn_fc1) &&
+            esm::make_tmap_f16(&c->tm_w2, c->w216, d, F, F, c->bn_fc2);
+  if (ok && c->has_head) ok = esm::make_tmap_f16(&c->tm_dense, c->dense16, d, d, d, c->bn_dense);
+  return ok ? ESM_OK : fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for a weight matrix");
+}
+
+int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* const* tensors, const size_t* sizes) {
+  std::string why;
+  if (dtype < 0 || dtype > 2) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0 or Q4_0");
+  if (!shape_supported(cfg, &why)) return fail(c, ESM_EINVAL, "unsupported model shape: " + why);
+  int64_t expect[ESM_NUM_TENSORS];
+  esm::tensor_layout(cfg, dtype, expect);
+  for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
+    if (tensors[i] == nullptr && !(i == 19 && sizes[i] == 0))
+      return fail(c, ESM_EINVAL, "tensor " + std::to_string(i) + " is null");
+    if (i < 19 && static_cast<int64_t>(sizes[i]) != expect[i])
+      return fail(c, ESM_EFORMAT, "tensor " + std::to_string(i) + " has " + std::to_string(sizes[i]) +
+                                      " bytes, expected " + std::to_string(expect[i]));
+  }
+  if (sizes[19] % 4) return fail(c, ESM_EFORMAT, "classifier byte size is not a multiple of 4");
+
+  ESM_CUDA(cudaSetDevice(c->device));
+  ESM_CUDA(cudaStreamSynchronize(c->stream));
+  free_list(c->w_allocs);
+  const bool same_shape = c->cfg.dim == cfg.dim && c->cfg.hidden_dim == cfg.hidden_dim &&
+                          c->cfg.n_heads == cfg.n_heads && c->cfg.n_layers == cfg.n_layers &&
+                          c->cfg.vocab_size == cfg.vocab_size;
+  if (!same_shape) {
+    // The workspace is sized for the previous shape: drop it (esm_reserve is required again).
+    free_list(c->ws_allocs);
+    free_pinned(c);
+    c->cap_tokens = 0;
+    c->plan_key.clear();
+  }
+  c->loaded = false;
+  c->cfg = cfg;
+  c->dtype = dtype;
+  const int64_t d = cfg.dim, F = cfg.hidden_dim, nl = cfg.n_layers, V = cfg.vocab_size;
+
+  for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
+    uint8_t* p = nullptr;
+    int rc = dev_alloc(c, c->w_allocs, &p, std::max<size_t>(sizes[i], 16));
+    if (rc) return rc;
+    if (sizes[i]) ESM_CUDA(cudaMemcpy(p, tensors[i], sizes[i], cudaMemcpyHostToDevice));
+    c->w[i] = p;
+  }
+  c->classifier_floats = static_cast<int64_t>(sizes[19] / 4);
+  c->has_head = c->classifier_floats >= esm::lm_head_floats(cfg);
+
+  // Stacked q|k|v bias per layer.
+  {
+    std::vector<float> hb(static_cast<size_t>(nl * 3 * d));
+    const float* bq = static_cast<const float*>(tensors[4]);
+    const float* bk = static_cast<const float*>(tensors[6]);
+    const float* bv = static_cast<const float*>(tensors[8]);
+    for (int64_t l = 0; l < nl; ++l) {
+      std::memcpy(&hb[l * 3 * d], bq + l * d, d * 4);
+      std::memcpy(&hb[l * 3 * d + d], bk + l * d, d * 4);
+      std::memcpy(&hb[l * 3 * d + 2 * d], bv + l * d, d * 4);
+    }
+    int rc = dev_alloc(c, c->w_allocs, &c->bqkv, hb.size());
+    if (rc) return rc;
+    ESM_CUDA(cudaMemcpy(c->bqkv, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice));
+  }
+  if (dtype == ESM_DTYPE_Q8_0) {
+    int rc = dev_alloc(c, c->w_allocs, &c->emb_f32, static_cast<size_t>(V * d));
+    if (rc) return rc;
+    ESM_CUDA(esm::launch_to_f32(ESM_DTYPE_Q8_0, c->w[0], V * d, c->emb_f32, c->stream));
+  } else {
+    c->emb_f32 = static_cast<float*>(c->w[0]);
+  }
+  if (c->has_head) {
+    int rc = dev_alloc(c, c->w_allocs, &c->dense16, static_cast<size_t>(d * d));
+    if (rc) return rc;
+    const float* dense_w = static_cast<const float*>(c->w[19]) + 2 * d;
+    ESM_CUDA(esm::launch_to_f16(ESM_DTYPE_FP32, dense_w, d * d, c->dense16, c->stream));
+  }
+  int rc = dev_alloc(c, c->w_allocs, &c->wqkv16, static_cast<size_t>(3 * d * d));
+  if (!rc) rc = dev_alloc(c, c->w_allocs, &c->wo16, static_cast<size_t>(d * d));
+  if (!rc) rc = dev_alloc(c, c->w_allocs, &c->w116, static_cast<size_t>(F * d));
+  if (!rc) rc = dev_alloc(c, c->w_allocs, &c->w216, static_cast<size_t>(d * F));
+  if (rc) return rc;
+  rc = build_weight_maps(c);
+  if (rc) return rc;
+  ESM_CUDA(cudaStreamSynchronize(c->stream));
+  c->loaded = true;
+  // A previous contact head only fits if the shape is unchanged.
+  if (c->has_ch) {
+    cudaFree(c->d_ch_w);
+    c->d_ch_w = nullptr;
+    c->has_ch = false;
+  }
+  return ESM_OK;
+}
+
+// RoPE tables exactly as BidirectionalRunState::new (src/lib.rs:2510-2522), in f32 on the host.
+std::vector<float2> rope_table(int max_len, int head_dim) {
+  const int half = head_dim / 2;
+  std::vector<float2> t(static_cast<size_t>(max_len) * half);
+  for (int pos = 0; pos < max_len; ++pos) {
+    for (int j = 0; j < half; ++j) {
+      const float freq = 1.0f / std::pow(10000.0f, static_cast<float>(j * 2) / static_cast<float>(head_dim));
+      const float val = static_cast<float>(pos) * freq;
+      t[static_cast<size_t>(pos) * half + j] = make_float2(std::cos(val), std::sin(val));
+    }
+  }
+  return t;
+}
+
+int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool contacts) {
+  if (!c->loaded) return fail(c, ESM_EINVAL, "load weights before reserving the workspace");
+  if (max_tokens <= 0 || max_seqs <= 0 || max_len <= 0) return fail(c, ESM_EINVAL, "non-positive capacity");
+  ESM_CUDA(cudaSetDevice(c->device));
+  ESM_CUDA(cudaStreamSynchronize(c->stream));
+  free_list(c->ws_allocs);
+  free_pinned(c);
+  c->cap_tokens = 0;
+  const esm_config& g = c->cfg;
+  const int64_t d = g.dim, F = g.hidden_dim, H = g.n_heads, nl = g.n_layers;
+  const int64_t rows = (static_cast<int64_t>(max_tokens) + 127) / 128 * 128;
+  const int64_t full_seqs = max_tokens / max_len + 1;
+  const int64_t t_per = (max_len + 63) / 64;
+  const int64_t n_max = std::max(max_len - 2, 0);
+  c->cap_rows = rows;
+  c->work_cap = max_tokens / 64 + max_seqs + 1;
+  c->tiles_cap = contacts ? std::min<int64_t>(full_seqs, max_seqs) * t_per * t_per + 1 : 1;
+  c->m_cap = contacts ? std::min<int64_t>(full_seqs, max_seqs) * n_max * n_max + 1 : 1;
+  c->r_cap = contacts ? nl * H * static_cast<int64_t>(max_tokens) + 1 : 1;
+
+  int rc = ESM_OK;
+  auto A = [&](auto** p, size_t n) {
+    if (!rc) rc = dev_alloc(c, c->ws_allocs, p, n);
+  };
+  A(&c->x, rows * d);
+  A(&c->xn, rows * d);
+  A(&c->qkv, rows * 3 * d);
+  A(&c->ao, rows * d);
+  A(&c->hb, rows * F);
+  A(&c->headf, rows * d);
+  A(&c->hidden, rows * d);
+  A(&c->logits, rows * g.vocab_size);
+  A(&c->pos, rows);
+  A(&c->seq_of, rows);
+  A(&c->tokens, rows);
+  A(&c->cu, max_seqs + 1);
+  A(&c->escale, max_seqs);
+  A(&c->work, c->work_cap);
+  A(&c->ctiles, c->tiles_cap);
+  A(&c->m_off, max_seqs);
+  A(&c->r_off, max_seqs);
+  A(&c->rope, static_cast<size_t>(max_len) * (d / H / 2));
+  if (contacts) {
+    A(&c->lse, H * rows);
+    A(&c->M, c->m_cap);
+    A(&c->cmap, c->m_cap);
+    A(&c->r, c->r_cap);
+    A(&c->a_scr, static_cast<size_t>(max_seqs) * nl * H);
+  }
+  if (rc) return rc;
+  // Stale rows past T are read by the GEMM A-loads of a partial last tile; keep them finite.
+  ESM_CUDA(cudaMemset(c->xn, 0, rows * d * 2));
+  ESM_CUDA(cudaMemset(c->ao, 0, rows * d * 2));
+  ESM_CUDA(cudaMemset(c->hb, 0, rows * F * 2));
+  {
+    std::vector<float2> rt = rope_table(max_len, static_cast<int>(d / H));
+    ESM_CUDA(cudaMemcpy(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  }
+  ESM_CUDA(cudaMallocHost(&c->h_cu, sizeof(int32_t) * (max_seqs + 1)));
+  ESM_CUDA(cudaMallocHost(&c->h_work, sizeof(int2) * c->work_cap));
+  ESM_CUDA(cudaMallocHost(&c->h_tiles, sizeof(int4) * c->tiles_cap));
+  ESM_CUDA(cudaMallocHost(&c->h_moff, sizeof(int64_t) * max_seqs));
+  ESM_CUDA(cudaMallocHost(&c->h_roff, sizeof(int64_t) * max_seqs));
+  bool ok = esm::make_tmap_f16(&c->tm_xn, c->xn, rows, d, d, 128) &&
+            esm::make_tmap_f16(&c->tm_ao, c->ao, rows, d, d, 128) &&
+            esm::make_tmap_f16(&c->tm_hb, c->hb, rows, F, F, 128);
+  if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
+  c->cap_tokens = max_tokens;
+  c->cap_seqs = max_seqs;
+  c->cap_len = max_len;
+  c->cap_contacts = contacts;
+  c->plan_key.clear();
+  return ESM_OK;
+}
+
+// Builds and uploads the per-call plan (cu_seqlens, attention work list, contact tiles and
+// offsets). Identical consecutive plans are not re-uploaded.
+int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStream_t s) {
+  std::vector<int32_t> key(h_cu, h_cu + B + 1);
+  key.push_back(contacts ? 1 : 0);
+  if (key == c->plan_key) return ESM_OK;
+  const esm_config& g = c->cfg;
+  const int64_t hl = static_cast<int64_t>(g.n_layers) * g.n_heads;
+  // The previous plan's copies must have left the pinned staging before it is rewritten.
+  if (c->plan_ev) ESM_CUDA(cudaEventSynchronize(c->plan_ev));
+  int nw = 0, nt = 0;
+  int64_t moff = 0, roff = 0;
+  for (int b = 0; b <= B; ++b) c->h_cu[b] = h_cu[b];
+  for (int b = 0; b < B; ++b) {
+    const int len = h_cu[b + 1] - h_cu[b];
+    const int qt = (len + 63) / 64;
+    if (nw + qt > c->work_cap) return fail(c, ESM_ECAPACITY, "attention work list exceeds the reserved capacity");
+    for (int t = 0; t < qt; ++t) c->h_work[nw++] = make_int2(b, t);
+    if (contacts) {
+      const int64_t n = std::max(len - 2, 0);
+      c->h_moff[b] = moff;
+      c->h_roff[b] = roff;
+      moff += n * n;
+      roff += hl * n;
+      if (n > 0) {
+        if (nt + static_cast<int64_t>(qt) * qt > c->tiles_cap)
+          return fail(c, ESM_ECAPACITY, "contact tiles exceed the reserved capacity");
+        for (int i = 0; i < qt; ++i)
+          for (int j = 0; j < qt; ++j) c->h_tiles[nt++] = make_int4(b, i, j, 0);
+      }
+    }
+  }
+  if (contacts && (moff > c->m_cap || roff > c->r_cap))
+    return fail(c, ESM_ECAPACITY, "contact maps exceed the reserved capacity");
+  ESM_CUDA(cudaMemcpyAsync(c->cu, c->h_cu, sizeof(int32_t) * (B + 1), cudaMemcpyHostToDevice, s));
+  ESM_CUDA(cudaMemcpyAsync(c->work, c->h_work, sizeof(int2) * nw, cudaMemcpyHostToDevice, s));
+  if (contacts) {
+    ESM_CUDA(cudaMemcpyAsync(c->m_off, c->h_moff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
+    ESM_CUDA(cudaMemcpyAsync(c->r_off, c->h_roff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
+    if (nt) ESM_CUDA(cudaMemcpyAsync(c->ctiles, c->h_tiles, sizeof(int4) * nt, cudaMemcpyHostToDevice, s));
+  }
+  if (!c->plan_ev) ESM_CUDA(cudaEventCreateWithFlags(&c->plan_ev, cudaEventDisableTiming));
+  ESM_CUDA(cudaEventRecord(c->plan_ev, s));
+  c->plan_key = key;
+  c->plan_work = nw;
+  c->plan_tiles = nt;
+  return ESM_OK;
+}
+
+int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int M, int N, int K,
+         const float* bias, void* out, int ldo, cudaStream_t s) {
+  esm::GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.bias = bias;
+  p.out = out;
+  p.ldo = ldo;
+  p.pos = c->pos;
+  p.rope = c->rope;
+  p.rope_cols = 2 * c->cfg.dim;
+  p.err = c->d_err;
+  const int dh = c->cfg.dim / c->cfg.n_heads;
+  ESM_CUDA(esm::gemm_launch(ta, tb, bn, epi, epi == esm::kEpiQkvRope ? dh : 0, p, c->num_sms, s));
+  return ESM_OK;
+}
+
+// The forward over packed device tokens. Caller holds the context lock and validated shapes.
+int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B, float* d_logits, float* d_hidden,
+                 float* d_contacts, float* d_layer_hidden, cudaStream_t s) {
+  const esm_config& g = c->cfg;
+  const int d = g.dim, F = g.hidden_dim, H = g.n_heads, nl = g.n_layers, V = g.vocab_size;
+  const int dh = d / H;
+  const int T = h_cu[B];
+  const bool contacts = d_contacts != nullptr;
+  int rc = upload_plan(c, h_cu, B, contacts, s);
+  if (rc) return rc;
+
+  const float* ln1_w = static_cast<const float*>(c->w[1]);
+  const float* ln1_b = static_cast<const float*>(c->w[2]);
+  const float* bo = static_cast<const float*>(c->w[10]);
+  const float* ln2_w = static_cast<const float*>(c->w[11]);
+  const float* ln2_b = static_cast<const float*>(c->w[12]);
+  const float* fc1_b = static_cast<const float*>(c->w[14]);
+  const float* fc2_b = static_cast<const float*>(c->w[16]);
+  const float* lnf_w = static_cast<const float*>(c->w[17]);
+  const float* lnf_b = static_cast<const float*>(c->w[18]);
+  const int64_t dd = static_cast<int64_t>(d) * d, fd = static_cast<int64_t>(F) * d;
+  const int64_t mat_b = esm::matrix_bytes(c->dtype, dd), fc_b = esm::matrix_bytes(c->dtype, fd);
+
+  ESM_CUDA(esm::launch_seq_setup(d_tokens, c->cu, B, c->pos, c->seq_of, c->escale, s));
+  ESM_CUDA(esm::launch_embed_ln(d_tokens, c->seq_of, c->escale, c->dtype == ESM_DTYPE_Q8_0 ? nullptr : c->emb_f32,
+                                c->w[0], T, d, ln1_w, ln1_b, c->x, c->xn, s));
+  int64_t m_total = 0, r_total = 0;
+  if (contacts) {
+    for (int b = 0; b < B; ++b) {
+      const int64_t n = std::max(h_cu[b + 1] - h_cu[b] - 2, 0);
+      m_total += n * n;
+      r_total += static_cast<int64_t>(nl) * H * n;
+    }
+    ESM_CUDA(cudaMemsetAsync(c->M, 0, std::max<int64_t>(m_total, 1) * 4, s));
+    ESM_CUDA(cudaMemsetAsync(c->r, 0, std::max<int64_t>(r_total, 1) * 4, s));
+  }
+
+  esm::AttnParams ap{};
+  ap.qkv = c->qkv;
+  ap.out = c->ao;
+  ap.lse = contacts ? c->lse : nullptr;
+  ap.cu_seqlens = c->cu;
+  ap.work = c->work;
+  ap.n_work = c->plan_work;
+  ap.T = T;
+  ap.d = d;
+  ap.H = H;
+  ap.dh = dh;
+  ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
+
+  for (int l = 0; l < nl; ++l) {
+    esm::LayerSrc src{};
+    src.dtype = c->dtype;
+    src.w[0] = static_cast<const uint8_t*>(c->w[3]) + l * mat_b;
+    src.w[1] = static_cast<const uint8_t*>(c->w[5]) + l * mat_b;
+    src.w[2] = static_cast<const uint8_t*>(c->w[7]) + l * mat_b;
+    src.w[3] = static_cast<const uint8_t*>(c->w[9]) + l * mat_b;
+    src.w[4] = static_cast<const uint8_t*>(c->w[13]) + l * fc_b;
+    src.w[5] = static_cast<const uint8_t*>(c->w[15]) + l * fc_b;
+    src.elems[0] = src.elems[1] = src.elems[2] = src.elems[3] = dd;
+    src.elems[4] = src.elems[5] = fd;
+    ESM_CUDA(esm::launch_dequant_layer(src, c->wqkv16, c->wo16, c->w116, c->w216, s));
+    if (l > 0) ESM_CUDA(esm::launch_layernorm(c->x, T, d, ln1_w + l * d, ln1_b + l * d, c->xn, d, nullptr, s));
+    rc = gemm(c, c->tm_xn, c->tm_wqkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d, c->bqkv + static_cast<int64_t>(l) * 3 * d,
+              c->qkv, 3 * d, s);
+    if (rc) return rc;
+    ESM_CUDA(esm::launch_attention(ap, s));
+    if (contacts) {
+      esm::ContactParams cp{};
+      cp.qkv = c->qkv;
+      cp.lse = c->lse;
+      cp.cu_seqlens = c->cu;
+      cp.tiles = c->ctiles;
+      cp.n_tiles = c->plan_tiles;
+      cp.T = T;
+      cp.d = d;
+      cp.H = H;
+      cp.dh = dh;
+      cp.scale = ap.scale;
+      cp.w_layer = c->d_ch_w + static_cast<int64_t>(l) * H;
+      cp.m_off = c->m_off;
+      cp.M = c->M;
+      cp.r_off = c->r_off;
+      cp.r = c->r;
+      cp.head_base = l * H;
+      ESM_CUDA(esm::launch_contact_accumulate(cp, s));
+    }
+    rc = gemm(c, c->tm_ao, c->tm_wo, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d, s);
+    if (rc) return rc;
+    ESM_CUDA(esm::launch_layernorm(c->x, T, d, ln2_w + l * d, ln2_b + l * d, c->xn, d, nullptr, s));
+    rc = gemm(c, c->tm_xn, c->tm_w1, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb, F,
+              s);
+    if (rc) return rc;
+    rc = gemm(c, c->tm_hb, c->tm_w2, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x, d,
+              s);
+    if (rc) return rc;
+    if (d_layer_hidden)
+      ESM_CUDA(cudaMemcpyAsync(d_layer_hidden + static_cast<int64_t>(l) * T * d, c->x, static_cast<size_t>(T) * d * 4,
+                               cudaMemcpyDeviceToDevice, s));
+  }
+
+  if (contacts) {
+    int max_n = 0;
+    for (int b = 0; b < B; ++b) max_n = std::max(max_n, h_cu[b + 1] - h_cu[b] - 2);
+    ESM_CUDA(esm::launch_contact_finalize(c->M, c->r, c->m_off, c->r_off, c->cu, B, max_n, nl * H, c->d_ch_w, c->ch_b,
+                                          c->a_scr, d_contacts, s));
+  }
+
+  // Final LayerNorm (state.x after the call), then the LM head (src/lib.rs:5379-5439).
+  float* hid32 = d_hidden ? d_hidden : (c->has_head ? nullptr : c->hidden);
+  ESM_CUDA(esm::launch_layernorm(c->x, T, d, lnf_w, lnf_b, c->xn, d, hid32, s));
+  if (c->has_head) {
+    const float* cls = static_cast<const float*>(c->w[19]);
+    const float* lm_ln_w = cls;
+    const float* lm_ln_b = cls + d;
+    const float* dense_b = cls + 2 * d + dd;
+    const float* dec_w = cls + 3 * d + dd;
+    const float* dec_b = dec_w + static_cast<int64_t>(V) * d;
+    rc = gemm(c, c->tm_xn, c->tm_dense, c->bn_dense, esm::kEpiGeluF32, T, d, d, dense_b, c->headf, d, s);
+    if (rc) return rc;
+    ESM_CUDA(esm::launch_lm_decoder(c->headf, T, d, 1, lm_ln_w, lm_ln_b, dec_w, dec_b, V, d_logits, s));
+  } else {
+    // Tied-embedding fallback: logits = x E^T with zero bias (src/lib.rs:5429-5439).
+    ESM_CUDA(esm::launch_lm_decoder(hid32, T, d, 0, nullptr, nullptr, c->emb_f32, nullptr, V, d_logits, s));
+  }
+  return ESM_OK;
+}
+
+int check_device_word(esm_ctx* c) {
+  int h = 0;
+  ESM_CUDA(cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h != 0) {
+    cudaMemset(c->d_err, 0, sizeof(int));
+    return fail(c, ESM_ETIMEOUT, "a device-side bounded wait gave up (code " + std::to_string(h) + ")");
+  }
+  return ESM_OK;
+}
+
+int validate_call(esm_ctx* c, const int32_t* h_cu, int B, bool contacts) {
+  if (!c->loaded) return fail(c, ESM_EINVAL, "no weights loaded");
+  if (c->cap_tokens == 0) return fail(c, ESM_EINVAL, "call esm_reserve before the first forward");
+  if (B <= 0) return fail(c, ESM_EINVAL, "batch must hold at least one sequence");
+  if (B > c->cap_seqs) return fail(c, ESM_ECAPACITY, "batch exceeds the reserved number of sequences");
+  if (h_cu[0] != 0) return fail(c, ESM_EINVAL, "cu_seqlens must start at 0");
+  for (int b = 0; b < B; ++b) {
+    const int len = h_cu[b + 1] - h_cu[b];
+    if (len <= 0) return fail(c, ESM_EINVAL, "sequence " + std::to_string(b) + " is empty");
+    if (len > c->cap_len)
+      return fail(c, ESM_ECAPACITY, "Sequence length " + std::to_string(len) + " exceeds max_len " +
+                                        std::to_string(c->cap_len));
+  }
+  if (h_cu[B] > c->cap_tokens) return fail(c, ESM_ECAPACITY, "token count exceeds the reserved capacity");
+  if (contacts && !c->cap_contacts) return fail(c, ESM_ECAPACITY, "workspace was reserved without contact maps");
+  if (contacts && !c->has_ch) return fail(c, ESM_EINVAL, "contacts requested but no contact head was set");
+  return ESM_OK;
+}
+
+bool read_exact(std::ifstream& f, void* dst, size_t n) {
+  f.read(static_cast<char*>(dst), static_cast<std::streamsize>(n));
+  return static_cast<size_t>(f.gcount()) == n;
+}
+
+bool path_hint(const std::string& p, const char* tag) { return p.find(tag) != std::string::npos; }
+
+}  // namespace
+
+extern "C" {
+
+int esm_config_preset(int32_t arch, esm_config* out) {
+  if (!out || !esm::config_preset(arch, out)) return ESM_EINVAL;
+  return ESM_OK;
+}
+
+int esm_config_detect_file(const char* path, esm_config* out, int32_t* dtype) {
+  if (!path || !out) return ESM_EINVAL;
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f) return ESM_EIO;
+  const uint64_t len = static_cast<uint64_t>(f.tellg());
+  f.seekg(0);
+  if (len >= 64) {
+    CodqHeader h;
+    if (read_exact(f, &h, 64) && std::memcmp(h.magic, "CODQ", 4) == 0) {
+      if (!h.validate(nullptr).empty()) return ESM_EFORMAT;
+      esm::config_preset(static_cast<int>(h.arch), out);
+      if (dtype) *dtype = static_cast<int32_t>(h.dtype);
+      return ESM_OK;
+    }
+  }
+  if (!esm::detect_from_file_len(len, out)) return ESM_EFORMAT;
+  if (dtype) *dtype = ESM_DTYPE_FP32;
+  return ESM_OK;
+}
+
+int esm_quantize_q8(const float* src, int64_t n, void* dst) {
+  if (!src || !dst || n < 0 || n % 32) return ESM_EINVAL;
+  esm::quantize_q8(src, n, static_cast<uint8_t*>(dst));
+  return ESM_OK;
+}
+
+int esm_quantize_q4(const float* src, int64_t n, void* dst) {
+  if (!src || !dst || n < 0 || n % 32) return ESM_EINVAL;
+  esm::quantize_q4(src, n, static_cast<uint8_t*>(dst));
+  return ESM_OK;
+}
+
+int esm_tokenize(const char* seq, int32_t* out, int32_t cap, int32_t* n_out) {
+  if (!seq || !n_out || (!out && cap > 0)) return ESM_EINVAL;
+  return esm::tokenize(seq, out, cap, n_out);
+}
+
+int esm_ctx_create(int32_t device, esm_ctx** out) {
+  if (!out) return ESM_EINVAL;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return ESM_ECUDA;
+  if (device < 0 || device >= n) return ESM_EINVAL;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return ESM_ECUDA;
+  if (prop.major != 10) return ESM_EINVAL;  // built for sm_100a only
+  esm_ctx* c = new esm_ctx();
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+    delete c;
+    return ESM_ECUDA;
+  }
+  *out = c;
+  return ESM_OK;
+}
+
+int esm_ctx_destroy(esm_ctx* c) {
+  if (!c) return ESM_EINVAL;
+  {
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    free_list(c->w_allocs);
+    free_list(c->ws_allocs);
+    free_pinned(c);
+    if (c->d_ch_w) cudaFree(c->d_ch_w);
+    if (c->d_padded_tokens) cudaFree(c->d_padded_tokens);
+    if (c->d_padded_out) cudaFree(c->d_padded_out);
+    if (c->plan_ev) cudaEventDestroy(c->plan_ev);
+    if (c->d_err) cudaFree(c->d_err);
+    cudaStreamDestroy(c->stream);
+  }
+  delete c;
+  return ESM_OK;
+}
+
+const char* esm_last_error(const esm_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+int esm_load_host(esm_ctx* c, const esm_config* cfg, int32_t dtype, const void* const* tensors, const size_t* sizes) {
+  if (!c || !cfg || !tensors || !sizes) return fail(c, ESM_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  return load_host_impl(c, *cfg, dtype, tensors, sizes);
+}
+
+int esm_load_file(esm_ctx* c, const char* path, const esm_config* cfg_in) {
+  if (!c || !path) return fail(c, ESM_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f) return fail(c, ESM_EIO, std::string("cannot open ") + path);
+  const uint64_t file_len = static_cast<uint64_t>(f.tellg());
+  f.seekg(0);
+  esm_config cfg{};
+  int dtype = ESM_DTYPE_FP32;
+  uint64_t start = 0;
+  CodqHeader h{};
+  const bool has_header = file_len >= 64 && read_exact(f, &h, 64) && std::memcmp(h.magic, "CODQ", 4) == 0;
+  if (has_header) {
+    const std::string why = h.validate(cfg_in);
+    if (!why.empty()) return fail(c, ESM_EFORMAT, why);
+    esm::config_preset(static_cast<int>(h.arch), &cfg);
+    dtype = static_cast<int>(h.dtype);
+    if (dtype > ESM_DTYPE_Q4_0) return fail(c, ESM_EFORMAT, "unsupported CODQ dtype " + std::to_string(dtype));
+    start = 64;
+  } else {
+    if (cfg_in) {
+      cfg = *cfg_in;
+    } else if (!esm::detect_from_file_len(file_len, &cfg)) {
+      esm::config_preset(0, &cfg);  // load_from_file falls back to the 8M config
+    }
+    // Header-less Q8_0/Q4_0 files are recognised by name, as load_or_convert does
+    // (src/lib.rs:838-856, 1250-1274); everything else is FP32.
+    const std::string p(path);
+    if (path_hint(p, "q4")) dtype = ESM_DTYPE_Q4_0;
+    else if (path_hint(p, "q8")) dtype = ESM_DTYPE_Q8_0;
+  }
+  const uint64_t remaining = file_len - start;
+  std::vector<uint8_t> buf(remaining);
+  f.clear();
+  f.seekg(static_cast<std::streamoff>(start));
+  if (!read_exact(f, buf.data(), remaining)) return fail(c, ESM_EIO, "short read");
+
+  int64_t sz[ESM_NUM_TENSORS];
+  esm::tensor_layout(cfg, dtype, sz);
+  const void* ptr[ESM_NUM_TENSORS];
+  size_t sizes[ESM_NUM_TENSORS];
+  std::vector<float> reordered;
+  if (dtype == ESM_DTYPE_FP32) {
+    if (remaining % 4) return fail(c, ESM_EFORMAT, "Unaligned trailing bytes: not a multiple of 4");
+    const int64_t floats = static_cast<int64_t>(remaining / 4);
+    const int64_t d = cfg.dim, F = cfg.hidden_dim, nl = cfg.n_layers, V = cfg.vocab_size;
+    if (floats == esm::grouped_canonical_floats(cfg)) {
+      sz[19] = esm::lm_head_floats(cfg) * 4;
+      uint64_t off = 0;
+      for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
+        ptr[i] = buf.data() + off;
+        sizes[i] = static_cast<size_t>(sz[i]);
+        off += sz[i];
+      }
+    } else if (floats == esm::sequential_hf_floats(cfg)) {
+      // Sequential HF / fair-esm dump (src/lib.rs:397-489): per-layer q,bq,k,bk,v,bv,o,bo,ln1 w/b,
+      // fc1 w/b, fc2 w/b, ln2 w/b; then ln_f, contact head, lm bias, dense w/b, lm ln w/b, decoder.
+      const float* s = reinterpret_cast<const float*>(buf.data());
+      int64_t total = 0;
+      for (int i = 0; i < 19; ++i) total += sz[i] / 4;
+      total += esm::lm_head_floats(cfg);
+      reordered.resize(static_cast<size_t>(total));
+      int64_t off[ESM_NUM_TENSORS];
+      int64_t o = 0;
+      for (int i = 0; i < 19; ++i) {
+        off[i] = o;
+        o += sz[i] / 4;
+      }
+      off[19] = o;
+      float* r = reordered.data();
+      int64_t p = 0;
+      auto take = [&](float* dst, int64_t n) {
+        std::memcpy(dst, s + p, n * 4);
+        p += n;
+      };
+      take(r + off[0], V * d);
+      p += (d / cfg.n_heads) / 2;  // inv_freq
+      for (int64_t l = 0; l < nl; ++l) {
+        take(r + off[3] + l * d * d, d * d);
+        take(r + off[4] + l * d, d);
+        take(r + off[5] + l * d * d, d * d);
+        take(r + off[6] + l * d, d);
+        take(r + off[7] + l * d * d, d * d);
+        take(r + off[8] + l * d, d);
+        take(r + off[9] + l * d * d, d * d);
+        take(r + off[10] + l * d, d);
+        take(r + off[1] + l * d, d);
+        take(r + off[2] + l * d, d);
+        take(r + off[13] + l * F * d, F * d);
+        take(r + off[14] + l * F, F);
+        take(r + off[15] + l * d * F, d * F);
+        take(r + off[16] + l * d, d);
+        take(r + off[11] + l * d, d);
+        take(r + off[12] + l * d, d);
+      }
+      take(r + off[17], d);
+      take(r + off[18], d);
+      p += nl * cfg.n_heads + 1;  // contact head
+      float* cls = r + off[19];   // [lm_ln_w | lm_ln_b | dense_w | dense_b | dec_w | dec_b]
+      take(cls + 3 * d + d * d + V * d, V);
+      take(cls + 2 * d, d * d);
+      take(cls + 2 * d + d * d, d);
+      take(cls, d);
+      take(cls + d, d);
+      take(cls + 3 * d + d * d, V * d);
+      sz[19] = esm::lm_head_floats(cfg) * 4;
+      for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
+        ptr[i] = r + off[i];
+        sizes[i] = static_cast<size_t>(sz[i]);
+      }
+    } else {
+      return fail(c, ESM_EFORMAT,
+                  "Invalid FP32 weights size: found " + std::to_string(remaining) + " bytes, expected " +
+                      std::to_string(esm::grouped_canonical_floats(cfg) * 4) + " (grouped_canonical_v1) or " +
+                      std::to_string(esm::sequential_hf_floats(cfg) * 4) + " (sequential_hf)");
+    }
+  } else {
+    uint64_t off = 0;
+    for (int i = 0; i < 19; ++i) {
+      if (off + sz[i] > remaining) return fail(c, ESM_EIO, "weights file ends inside tensor " + std::to_string(i));
+      ptr[i] = buf.data() + off;
+      sizes[i] = static_cast<size_t>(sz[i]);
+      off += sz[i];
+    }
+    const uint64_t rest = remaining - off;
+    if (rest % 4) return fail(c, ESM_EFORMAT, "Unaligned trailing bytes: not a multiple of 4");
+    ptr[19] = buf.data() + off;
+    sizes[19] = static_cast<size_t>(rest);
+  }
+  return load_host_impl(c, cfg, dtype, ptr, sizes);
+}
+
+int esm_set_contact_head(esm_ctx* c, const float* w, int32_t nw, float b) {
+  if (!c || !w) return fail(c, ESM_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (!c->loaded) return fail(c, ESM_EINVAL, "load weights before setting the contact head");
+  if (nw != c->cfg.n_layers * c->cfg.n_heads)
+    return fail(c, ESM_EINVAL, "contact head needs n_layers * n_heads = " +
+                                   std::to_string(c->cfg.n_layers * c->cfg.n_heads) + " weights");
+  ESM_CUDA(cudaSetDevice(c->device));
+  if (!c->d_ch_w) ESM_CUDA(cudaMalloc(&c->d_ch_w, sizeof(float) * nw));
+  ESM_CUDA(cudaMemcpy(c->d_ch_w, w, sizeof(float) * nw, cudaMemcpyHostToDevice));
+  c->ch_b = b;
+  c->has_ch = true;
+  return ESM_OK;
+}
+
+int esm_reserve(esm_ctx* c, int32_t max_tokens, int32_t max_seqs, int32_t max_len, int32_t contacts) {
+  if (!c) return ESM_EINVAL;
+  std::lock_guard<std::mutex> lk(c->mu);
+  return reserve_impl(c, max_tokens, max_seqs, max_len, contacts != 0);
+}
+
+int esm_forward_device(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu_seqlens, int32_t B, float* d_logits,
+                       float* d_hidden, float* d_contacts, float* d_layer_hidden, void* stream, int32_t sync) {
+  if (!c || !d_tokens || !h_cu_seqlens || !d_logits) return fail(c, ESM_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  int rc = validate_call(c, h_cu_seqlens, B, d_contacts != nullptr);
+  if (rc) return rc;
+  ESM_CUDA(cudaSetDevice(c->device));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  rc = forward_impl(c, d_tokens, h_cu_seqlens, B, d_logits, d_hidden, d_contacts, d_layer_hidden, s);
+  if (rc) return rc;
+  if (sync) {
+    ESM_CUDA(cudaStreamSynchronize(s));
+    return check_device_word(c);
+  }
+  return ESM_OK;
+}
+
+int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax, float* logits,
+                float* hidden, float* contacts) {
+  if (!c || !tokens || !lengths || !logits) return fail(c, ESM_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (B <= 0 || Lmax <= 0) return fail(c, ESM_EINVAL, "empty batch");
+  std::vector<int32_t> cu(B + 1, 0);
+  for (int b = 0; b < B; ++b) {
+    if (lengths[b] <= 0 || lengths[b] > Lmax) return fail(c, ESM_EINVAL, "length outside [1, Lmax]");
+    cu[b + 1] = cu[b] + lengths[b];
+  }
+  int rc = validate_call(c, cu.data(), B, contacts != nullptr);
+  if (rc) return rc;
+  ESM_CUDA(cudaSetDevice(c->device));
+  cudaStream_t s = c->stream;
+  const esm_config& g = c->cfg;
+  const size_t ntok = static_cast<size_t>(B) * Lmax;
+  if (ntok > c->padded_tok_cap) {
+    if (c->d_padded_tokens) cudaFree(c->d_padded_tokens);
+    c->d_padded_tokens = nullptr;
+    c->padded_tok_cap = 0;
+    ESM_CUDA(cudaMalloc(&c->d_padded_tokens, ntok * sizeof(int32_t)));
+    c->padded_tok_cap = ntok;
+  }
+  const size_t np = Lmax > 2 ? static_cast<size_t>(Lmax - 2) : 0;
+  const size_t out_need = std::max({ntok * g.vocab_size, hidden ? ntok * g.dim : 0, contacts ? B * np * np : 0});
+  if (out_need > c->padded_out_cap) {
+    if (c->d_padded_out) cudaFree(c->d_padded_out);
+    c->d_padded_out = nullptr;
+    c->padded_out_cap = 0;
+    ESM_CUDA(cudaMalloc(&c->d_padded_out, out_need * sizeof(float)));
+    c->padded_out_cap = out_need;
+  }
+  // The plan (and with it cu_seqlens on the device) must be in place before the token gather.
+  rc = upload_plan(c, cu.data(), B, contacts != nullptr, s);
+  if (rc) return rc;
+  ESM_CUDA(cudaMemcpyAsync(c->d_padded_tokens, tokens, ntok * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  ESM_CUDA(esm::launch_gather_tokens(c->d_padded_tokens, c->cu, B, Lmax, c->tokens, s));
+  rc = forward_impl(c, c->tokens, cu.data(), B, c->logits, hidden ? c->hidden : nullptr, contacts ? c->cmap : nullptr,
+                    nullptr, s);
+  if (rc) return rc;
+  ESM_CUDA(esm::launch_scatter_rows(c->logits, c->cu, B, Lmax, g.vocab_size, c->d_padded_out, s));
+  ESM_CUDA(cudaMemcpyAsync(logits, c->d_padded_out, ntok * g.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, s));
+  if (hidden) {
+    ESM_CUDA(esm::launch_scatter_rows(c->hidden, c->cu, B, Lmax, g.dim, c->d_padded_out, s));
+    ESM_CUDA(cudaMemcpyAsync(hidden, c->d_padded_out, ntok * g.dim * sizeof(float), cudaMemcpyDeviceToHost, s));
+  }
+  if (contacts && np > 0) {
+    ESM_CUDA(esm::launch_scatter_maps(c->cmap, c->m_off, c->cu, B, Lmax, c->d_padded_out, s));
+    ESM_CUDA(cudaMemcpyAsync(contacts, c->d_padded_out, B * np * np * sizeof(float), cudaMemcpyDeviceToHost, s));
+  }
+  ESM_CUDA(cudaStreamSynchronize(s));
+  return check_device_word(c);
+}
+
+int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,
+                     int32_t out_dim, int32_t seq_len, float* out) {
+  if (!c || !x || !w || !out) return fail(c, ESM_EINVAL, "null argument");
+  if (dtype < 0 || dtype > 2) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0 or Q4_0");
+  if (in_dim <= 0 || in_dim % 32 || out_dim <= 0 || seq_len <= 0)
+    return fail(c, ESM_EINVAL, "in_dim must be a positive multiple of 32; out_dim and seq_len positive");
+  std::lock_guard<std::mutex> lk(c->mu);
+  ESM_CUDA(cudaSetDevice(c->device));
+  cudaStream_t s = c->stream;
+  const int n_pad = (out_dim + 15) / 16 * 16;
+  const int bn = esm::gemm_pick_bn_any(n_pad);
+  const int64_t rows = (static_cast<int64_t>(seq_len) + 127) / 128 * 128;
+  const int64_t wbytes = esm::matrix_bytes(dtype, static_cast<int64_t>(out_dim) * in_dim);
+  std::vector<void*> tmp;
+  float *x32 = nullptr, *b32 = nullptr, *o32 = nullptr;
+  __half *x16 = nullptr, *w16 = nullptr;
+  uint8_t* wd = nullptr;
+  int rc = dev_alloc(c, tmp, &x32, static_cast<size_t>(seq_len) * in_dim);
+  if (!rc) rc = dev_alloc(c, tmp, &x16, static_cast<size_t>(rows) * in_dim);
+  if (!rc) rc = dev_alloc(c, tmp, &wd, static_cast<size_t>(wbytes));
+  if (!rc) rc = dev_alloc(c, tmp, &w16, static_cast<size_t>(n_pad) * in_dim);
+  if (!rc) rc = dev_alloc(c, tmp, &b32, static_cast<size_t>(n_pad));
+  if (!rc) rc = dev_alloc(c, tmp, &o32, static_cast<size_t>(seq_len) * n_pad);
+  auto done = [&](int code) {
+    cudaStreamSynchronize(s);
+    free_list(tmp);
+    return code;
+  };
+  if (rc) return done(rc);
+  CUtensorMap ta, tb;
+  esm::GemmParams p{};
+  cudaError_t e = cudaMemsetAsync(x16, 0, rows * in_dim * 2, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w16, 0, static_cast<size_t>(n_pad) * in_dim * 2, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b32, 0, static_cast<size_t>(n_pad) * 4, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(x32, x, static_cast<size_t>(seq_len) * in_dim * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(wd, w, static_cast<size_t>(wbytes), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess && bias) e = cudaMemcpyAsync(b32, bias, static_cast<size_t>(out_dim) * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = esm::launch_to_f16(ESM_DTYPE_FP32, x32, static_cast<int64_t>(seq_len) * in_dim, x16, s);
+  if (e == cudaSuccess) e = esm::launch_to_f16(dtype, wd, static_cast<int64_t>(out_dim) * in_dim, w16, s);
+  if (e != cudaSuccess) return done(fail(c, ESM_ECUDA, std::string("matmul_tiled setup: ") + cudaGetErrorString(e)));
+  if (!esm::make_tmap_f16(&ta, x16, rows, in_dim, in_dim, 128) || !esm::make_tmap_f16(&tb, w16, n_pad, in_dim, in_dim, bn))
+    return done(fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed"));
+  p.M = seq_len;
+  p.N = n_pad;
+  p.K = in_dim;
+  p.bias = b32;
+  p.out = o32;
+  p.ldo = n_pad;
+  p.err = c->d_err;
+  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, c->num_sms, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(out, static_cast<size_t>(out_dim) * 4, o32, static_cast<size_t>(n_pad) * 4,
+                          static_cast<size_t>(out_dim) * 4, seq_len, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return done(fail(c, ESM_ECUDA, std::string("matmul_tiled: ") + cudaGetErrorString(e)));
+  return done(check_device_word(c));
+}
+
+int esm_check_device(esm_ctx* c) {
+  if (!c) return ESM_EINVAL;
+  std::lock_guard<std::mutex> lk(c->mu);
+  ESM_CUDA(cudaSetDevice(c->device));
+  ESM_CUDA(cudaStreamSynchronize(c->stream));
+  return check_device_word(c);
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Host-side interface of the tcgen05 GEMM used for every projection of the encoder.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace esm {
+
+// What the epilogue does with acc = A[m,:] . B[n,:] (fp32, from TMEM) for output element (m, n).
+enum GemmEpilogue : int {
+  kEpiQkvRope = 0,  // out f16 = rope(acc + bias) for n < rope_cols, acc + bias otherwise
+  kEpiGeluF16 = 1,  // out f16 = gelu(acc + bias)
+  kEpiResidF32 = 2, // out f32 += acc + bias            (residual stream update)
+  kEpiGeluF32 = 3,  // out f32 = gelu(acc + bias)
+  kEpiStoreF32 = 4, // out f32 = acc + bias
+};
+
+struct GemmParams {
+  int M, N, K;
+  int num_m_blocks, num_n_blocks;
+  const float* bias;    // [N], may be null
+  void* out;            // row-major, `ldo` elements per row
+  int ldo;
+  const int* pos;       // [M] token position inside its sequence (kEpiQkvRope)
+  const float2* rope;   // [max_pos, dh/2] (cos, sin) in f32 (kEpiQkvRope)
+  int rope_cols;        // columns [0, rope_cols) are rotated (kEpiQkvRope)
+  int* err;             // device error word
+};
+
+// Encodes a 2-D fp16 tensor map over a row-major [rows, cols] matrix with `ld` elements per row,
+// box = [box_rows, 64 columns], 128-byte swizzle, zero fill outside the matrix.
+bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                   uint32_t box_rows);
+
+// Largest supported tile width that divides N (and is a multiple of `head_dim` when non-zero).
+int gemm_pick_bn(int N, int head_dim);
+// Same, including the narrow widths (96..16) that only the kEpiStoreF32 epilogue supports.
+int gemm_pick_bn_any(int N);
+
+// C[M, N] = A[M, K] . B[N, K]^T with the requested epilogue; A and B are fp16 K-major behind the
+// tensor maps (A box 128 rows, B box `bn` rows). Persistent grid of min(tiles, num_sms) CTAs.
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int head_dim,
+                        GemmParams p, int num_sms, cudaStream_t stream);
+
+}  // namespace esm

@@ -1,0 +1,102 @@
+// Launchers of the memory-bound kernels around the GEMMs and of the attention kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace esm {
+
+// Quantized matrices stay on the device in their on-disk CODQ layout: arrays of BlockQ8_0
+// {f32 d; i8 qs[32]} (36 B) or BlockQ4_0 {f32 d; u8 qs[16]} (20 B, low nibble = element j, high
+// nibble = element j + 16, value = (q - 8) * d), 32 elements per block along the input dimension
+// (src/lib.rs:640-645, 1043-1051). Blocks are 4-byte aligned and read with 32-bit loads.
+constexpr int kQ8BlockBytes = 36;
+constexpr int kQ4BlockBytes = 20;
+
+// One layer's weight matrices for the dequantizing conversion to fp16 (dtype = ESM_DTYPE_*):
+// q, k, v, o, fc1, fc2 as fp32 arrays (dtype 0) or block arrays (dtype 1 / 2).
+struct LayerSrc {
+  int dtype;
+  const void* w[6];
+  int64_t elems[6];  // element count of each matrix
+};
+
+// Per-sequence bookkeeping: pos[t] (token index inside its sequence), seq_of[t], and the
+// token-dropout embedding scale of each sequence (src/lib.rs:5115-5117).
+cudaError_t launch_seq_setup(const int32_t* tokens, const int32_t* cu_seqlens, int B, int32_t* pos, int32_t* seq_of,
+                             float* embed_scale, cudaStream_t s);
+
+// x[t] = E[tok]*scale (0 for <mask>) in fp32, then xn = LN(x; ln_w, ln_b) in fp16.
+// E is fp32 [V, d] (emb_f32 != null) or BlockQ8_0 blocks [V, d/32] (emb_q8).
+cudaError_t launch_embed_ln(const int32_t* tokens, const int32_t* seq_of, const float* embed_scale,
+                            const float* emb_f32, const void* emb_q8, int T, int d, const float* ln_w,
+                            const float* ln_b, float* x, __half* xn, cudaStream_t s);
+
+// out16 = LN(x) in fp16 (row stride ld16) and, when out32 != null, also in fp32 ([T, d]).
+cudaError_t launch_layernorm(const float* x, int T, int d, const float* w, const float* b, __half* out16, int ld16,
+                             float* out32, cudaStream_t s);
+
+// Converts one layer's six weight matrices to fp16 (q|k|v stacked into wqkv).
+cudaError_t launch_dequant_layer(const LayerSrc& src, __half* wqkv, __half* wo, __half* w1, __half* w2,
+                                 cudaStream_t s);
+
+// Generic converter of a whole matrix (fp32 or blocks) to fp16 / fp32 (load-time use).
+cudaError_t launch_to_f16(int dtype, const void* src, int64_t elems, __half* dst, cudaStream_t s);
+cudaError_t launch_to_f32(int dtype, const void* src, int64_t elems, float* dst, cudaStream_t s);
+
+// Padded [B, Lmax] int32 tokens -> packed [T] following cu_seqlens.
+cudaError_t launch_gather_tokens(const int32_t* padded, const int32_t* cu_seqlens, int B, int Lmax, int32_t* packed,
+                                 cudaStream_t s);
+// Packed per-sequence n_b x n_b maps -> padded [B, Lmax-2, Lmax-2] (zero outside each map).
+cudaError_t launch_scatter_maps(const float* src, const int64_t* m_off, const int32_t* cu_seqlens, int B, int Lmax,
+                                float* dst, cudaStream_t s);
+
+// logits[t, :] = (do_ln ? LN(in[t]; ln_w, ln_b) : in[t]) . W^T + bias   (W fp32 [V, d], bias may be null)
+cudaError_t launch_lm_decoder(const float* in, int T, int d, int do_ln, const float* ln_w, const float* ln_b,
+                              const float* W, const float* bias, int V, float* logits, cudaStream_t s);
+
+// Packed rows [T, C] -> padded [B, Lmax, C] (padding rows zeroed).
+cudaError_t launch_scatter_rows(const float* src, const int32_t* cu_seqlens, int B, int Lmax, int C, float* dst,
+                                cudaStream_t s);
+
+// ---- attention ------------------------------------------------------------------------------
+struct AttnParams {
+  const __half* qkv;       // [T, 3d]: q | k | v, head h at columns h*dh of each part
+  __half* out;             // [T, d]
+  float* lse;              // [H, T] natural-log row log-sum-exp of the scaled scores, or null
+  const int32_t* cu_seqlens;
+  const int2* work;        // (sequence, 64-row query tile) pairs
+  int n_work;
+  int T, d, H, dh;
+  float scale;             // 1/sqrt(dh)
+};
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t s);
+
+// Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
+// recomputes P = softmax(q k^T * scale) tile by tile from the saved LSE, adds w * P into the
+// per-sequence accumulator M[n, n] (inner block, <cls>/<eos> removed) and the head's row and column
+// sums of P into r[head, n] (for APC). Nothing per-head is stored.
+struct ContactParams {
+  const __half* qkv;
+  const float* lse;        // [H, T]
+  const int32_t* cu_seqlens;
+  const int4* tiles;       // (sequence, i-tile, j-tile, unused) over each sequence's L x L map
+  int n_tiles;
+  int T, d, H, dh;
+  float scale;
+  const float* w_layer;    // [H] regression weights of this layer
+  const int64_t* m_off;    // [B] float offset of sequence b's M (and output map)
+  float* M;                // sum over heads of w * P (inner block)
+  const int64_t* r_off;    // [B] float offset of sequence b's r block ([n_heads_total, n_b])
+  float* r;
+  int head_base;           // layer * H
+};
+cudaError_t launch_contact_accumulate(const ContactParams& p, cudaStream_t s);
+
+// contacts = sigmoid(M + M^T - sum_h a_h r_h r_h^T + b) with a_h = w_h / T_h (APC), per sequence.
+cudaError_t launch_contact_finalize(const float* M, const float* r, const int64_t* m_off, const int64_t* r_off,
+                                    const int32_t* cu_seqlens, int B, int max_n, int n_heads_total, const float* w_all,
+                                    float bias, float* a_scratch, float* out, cudaStream_t s);
+
+}  // namespace esm

@@ -1,0 +1,351 @@
+"""Python front end of libesm_b200.so (ctypes over the C ABI in include/esm_b200.h).
+
+Mirrors codon-infer's model API for the encoder forward: EsmConfig presets, weight loading
+(host tensors in EsmWeights order, or CODQ / grouped_canonical_v1 files), the Q8_0/Q4_0
+quantizers, the tokenizer, and forward_bidirectional over a batch. The library is required: there
+is no CPU fallback, and loading fails loudly when it is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libesm_b200.so"
+
+ESM_OK, ESM_EINVAL, ESM_EFORMAT, ESM_ECAPACITY, ESM_ECUDA, ESM_ENCCL, ESM_ETIMEOUT, ESM_ENOMEM, ESM_EIO = range(9)
+DTYPE_FP32, DTYPE_Q8_0, DTYPE_Q4_0 = 0, 1, 2
+ARCH_8M, ARCH_35M, ARCH_150M, ARCH_650M, ARCH_3B = range(5)
+Q8_BLOCK_BYTES, Q4_BLOCK_BYTES = 36, 20
+MASK_ID = 32
+
+# EsmWeights field order (also the grouped_canonical_v1 / CODQ file order).
+TENSOR_NAMES = (
+    "tok_emb", "ln1_w", "ln1_b", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo",
+    "ln2_w", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "lnf_w", "lnf_b", "classifier",
+)
+MATRICES = ("wq", "wk", "wv", "wo", "fc1_w", "fc2_w")
+
+
+class EsmError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[esm error {code}] {msg}")
+        self.code = code
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("dim", "hidden_dim", "n_layers", "n_heads", "vocab_size", "max_seq_len", "arch")]
+
+
+@dataclass(frozen=True)
+class EsmConfig:
+    """EsmConfig (src/lib.rs:76-84)."""
+    dim: int
+    hidden_dim: int
+    n_layers: int
+    n_heads: int
+    vocab_size: int = 33
+    max_seq_len: int = 1024
+    arch: int = 0
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+    @staticmethod
+    def preset(arch: int) -> "EsmConfig":
+        c = _Config()
+        _check(lib().esm_config_preset(arch, ctypes.byref(c)), "esm_config_preset")
+        return EsmConfig(c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.vocab_size, c.max_seq_len, c.arch)
+
+    def c_struct(self) -> _Config:
+        return _Config(self.dim, self.hidden_dim, self.n_layers, self.n_heads, self.vocab_size, self.max_seq_len,
+                       self.arch)
+
+    def lm_head_floats(self) -> int:
+        d, V = self.dim, self.vocab_size
+        return 3 * d + d * d + V * d + V
+
+
+def esm2_8m() -> EsmConfig: return EsmConfig.preset(ARCH_8M)
+def esm2_35m() -> EsmConfig: return EsmConfig.preset(ARCH_35M)
+def esm2_150m() -> EsmConfig: return EsmConfig.preset(ARCH_150M)
+def esm2_650m() -> EsmConfig: return EsmConfig.preset(ARCH_650M)
+def esm2_3b() -> EsmConfig: return EsmConfig.preset(ARCH_3B)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with codon-infer_b200/build.py "
+                               "(there is no CPU fallback)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+        sig = {
+            "esm_config_preset": [i32, vp],
+            "esm_config_detect_file": [ctypes.c_char_p, vp, vp],
+            "esm_quantize_q8": [vp, i64, vp],
+            "esm_quantize_q4": [vp, i64, vp],
+            "esm_tokenize": [ctypes.c_char_p, vp, i32, vp],
+            "esm_ctx_create": [i32, vp],
+            "esm_ctx_destroy": [vp],
+            "esm_load_file": [vp, ctypes.c_char_p, vp],
+            "esm_load_host": [vp, vp, i32, vp, vp],
+            "esm_set_contact_head": [vp, vp, i32, f32],
+            "esm_reserve": [vp, i32, i32, i32, i32],
+            "esm_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
+            "esm_forward_device": [vp, vp, vp, i32, vp, vp, vp, vp, vp, i32],
+            "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
+            "esm_check_device": [vp],
+        }
+        for name, args in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        L.esm_last_error.argtypes = [vp]
+        L.esm_last_error.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, what: str, ctx=None) -> None:
+    if rc != ESM_OK:
+        msg = lib().esm_last_error(ctx).decode() if ctx else what
+        raise EsmError(rc, f"{what}: {msg}")
+
+
+def _p(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+# ---- quantizers / tokenizer ------------------------------------------------------------------
+
+def quantize_q8(x) -> np.ndarray:
+    """BlockQ8_0 blocks (36 bytes each) of a float32 array whose size is a multiple of 32."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(x.size // 32 * Q8_BLOCK_BYTES, dtype=np.uint8)
+    _check(lib().esm_quantize_q8(_p(x), x.size, _p(out)), "esm_quantize_q8")
+    return out
+
+
+def quantize_q4(x) -> np.ndarray:
+    """BlockQ4_0 blocks (20 bytes each) of a float32 array whose size is a multiple of 32."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(x.size // 32 * Q4_BLOCK_BYTES, dtype=np.uint8)
+    _check(lib().esm_quantize_q4(_p(x), x.size, _p(out)), "esm_quantize_q4")
+    return out
+
+
+def tokenize(seq: str) -> np.ndarray:
+    """Tokenizer::encode: <cls> + residue ids + <eos> (int32)."""
+    cap = len(seq.encode()) + 2
+    out = np.empty(cap, dtype=np.int32)
+    n = ctypes.c_int32(0)
+    _check(lib().esm_tokenize(seq.encode(), _p(out), cap, ctypes.byref(n)), "esm_tokenize")
+    return out[: n.value].copy()
+
+
+def detect_file(path: str) -> tuple[EsmConfig, int]:
+    c = _Config()
+    dt = ctypes.c_int32(0)
+    _check(lib().esm_config_detect_file(str(path).encode(), ctypes.byref(c), ctypes.byref(dt)), "detect_file")
+    return EsmConfig(c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.vocab_size, c.max_seq_len, c.arch), dt.value
+
+
+# ---- synthetic weights ---------------------------------------------------------------------------
+
+def synth_fp32_tensors(cfg: EsmConfig, seed: int = 0, std: float = 0.02, bias_std: float = 0.0,
+                       ln_jitter: float = 0.0, tie_decoder: bool = True, with_classifier: bool = True) -> dict:
+    """Seeded random-init ESM-2 weights in EsmWeights order (float32 numpy arrays).
+
+    Matrices and the embedding ~ N(0, std); biases ~ N(0, bias_std) (0 by default); LayerNorm
+    gamma = 1 + N(0, ln_jitter), beta = N(0, ln_jitter). The classifier is
+    [lm_ln_w | lm_ln_b | dense_w | dense_b | dec_w | dec_b] with dec_w a copy of the embedding
+    when tie_decoder (the ESM-2 LM head is tied to the token embedding).
+    """
+    rng = np.random.default_rng(seed)
+    d, F, nl, V = cfg.dim, cfg.hidden_dim, cfg.n_layers, cfg.vocab_size
+
+    def normal(n, s):
+        if s == 0.0:
+            return np.zeros(n, dtype=np.float32)
+        a = rng.standard_normal(n, dtype=np.float32)
+        a *= np.float32(s)
+        return a
+
+    def gamma(n):
+        return (np.ones(n, dtype=np.float32) + normal(n, ln_jitter)).astype(np.float32)
+
+    t = {}
+    t["tok_emb"] = normal(V * d, std)
+    t["ln1_w"] = gamma(nl * d)
+    t["ln1_b"] = normal(nl * d, ln_jitter)
+    for w, b in (("wq", "bq"), ("wk", "bk"), ("wv", "bv"), ("wo", "bo")):
+        t[w] = normal(nl * d * d, std)
+        t[b] = normal(nl * d, bias_std)
+    t["ln2_w"] = gamma(nl * d)
+    t["ln2_b"] = normal(nl * d, ln_jitter)
+    t["fc1_w"] = normal(nl * F * d, std)
+    t["fc1_b"] = normal(nl * F, bias_std)
+    t["fc2_w"] = normal(nl * d * F, std)
+    t["fc2_b"] = normal(nl * d, bias_std)
+    t["lnf_w"] = gamma(d)
+    t["lnf_b"] = normal(d, ln_jitter)
+    if with_classifier:
+        dec_w = t["tok_emb"].copy() if tie_decoder else normal(V * d, std)
+        t["classifier"] = np.concatenate([
+            gamma(d), normal(d, ln_jitter), normal(d * d, std), normal(d, bias_std), dec_w, normal(V, bias_std),
+        ]).astype(np.float32)
+    else:
+        t["classifier"] = np.zeros(0, dtype=np.float32)
+    return t
+
+
+def quantize_tensors(t: dict, dtype: int) -> dict:
+    """Applies EsmWeights::quantize_q8 / quantize_q4 (src/lib.rs:558-607): the six matrices become
+    blocks; for Q8_0 the token embedding is quantized too, for Q4_0 it stays FP32."""
+    if dtype == DTYPE_FP32:
+        return dict(t)
+    q = quantize_q8 if dtype == DTYPE_Q8_0 else quantize_q4
+    out = dict(t)
+    for m in MATRICES:
+        out[m] = q(t[m])
+    if dtype == DTYPE_Q8_0:
+        out["tok_emb"] = quantize_q8(t["tok_emb"])
+    return out
+
+
+def random_sequences(n: int, lengths, seed: int = 0) -> list[np.ndarray]:
+    """Token sequences <cls> + residues uniform over the 20 canonical ids 4..23 + <eos>."""
+    rng = np.random.default_rng(seed)
+    lens = [lengths] * n if np.isscalar(lengths) else list(lengths)
+    out = []
+    for L in lens:
+        s = np.empty(L, dtype=np.int32)
+        s[0], s[-1] = 0, 2
+        s[1:-1] = rng.integers(4, 24, size=L - 2, dtype=np.int32)
+        out.append(s)
+    return out
+
+
+def write_codq(path: str, cfg: EsmConfig, dtype: int, tensors: dict) -> None:
+    """Writes a CODQ v1 file (64-byte header + tensors in EsmWeights order), as
+    EsmWeightsQ8::save_to_file_with_header / EsmWeightsQ4::save_to_file do."""
+    hdr = np.zeros(64, dtype=np.uint8)
+    hdr[0:4] = np.frombuffer(b"CODQ", dtype=np.uint8)
+    hdr[4:32] = np.array([1, dtype, cfg.arch, cfg.n_layers, cfg.dim, cfg.hidden_dim, cfg.vocab_size],
+                         dtype="<u4").view(np.uint8)
+    with open(path, "wb") as f:
+        f.write(hdr.tobytes())
+        for n in TENSOR_NAMES:
+            f.write(np.ascontiguousarray(tensors[n]).tobytes())
+
+
+# ---- model ----------------------------------------------------------------------------------
+
+class Model:
+    """One context on one GPU: weights, contact head and workspace."""
+
+    def __init__(self, device: int = 0):
+        self._ctx = ctypes.c_void_p()
+        rc = lib().esm_ctx_create(device, ctypes.byref(self._ctx))
+        if rc != ESM_OK:
+            raise EsmError(rc, f"esm_ctx_create(device={device}) failed")
+        self.device = device
+        self.cfg: EsmConfig | None = None
+
+    def close(self) -> None:
+        if self._ctx:
+            lib().esm_ctx_destroy(self._ctx)
+            self._ctx = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _chk(self, rc: int, what: str) -> None:
+        if rc != ESM_OK:
+            raise EsmError(rc, f"{what}: {lib().esm_last_error(self._ctx).decode()}")
+
+    def load_tensors(self, cfg: EsmConfig, dtype: int, tensors: dict) -> None:
+        arrs = [np.ascontiguousarray(tensors[n]) for n in TENSOR_NAMES]
+        ptrs = (ctypes.c_void_p * 20)(*[a.ctypes.data if a.size else None for a in arrs])
+        sizes = (ctypes.c_size_t * 20)(*[a.nbytes for a in arrs])
+        c = cfg.c_struct()
+        self._chk(lib().esm_load_host(self._ctx, ctypes.byref(c), dtype, ptrs, sizes), "esm_load_host")
+        self.cfg = cfg
+
+    def load_file(self, path: str, cfg: EsmConfig | None = None) -> None:
+        c = cfg.c_struct() if cfg else None
+        self._chk(lib().esm_load_file(self._ctx, str(path).encode(), ctypes.byref(c) if c else None), "esm_load_file")
+        self.cfg = cfg or detect_file(path)[0]
+
+    def set_contact_head(self, w, b: float) -> None:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        self._chk(lib().esm_set_contact_head(self._ctx, _p(w), w.size, float(b)), "esm_set_contact_head")
+
+    def reserve(self, max_tokens: int, max_seqs: int, max_len: int, contacts: bool = False) -> None:
+        self._chk(lib().esm_reserve(self._ctx, max_tokens, max_seqs, max_len, int(contacts)), "esm_reserve")
+
+    def forward(self, seqs, want_hidden: bool = False, want_contacts: bool = False, out=None) -> dict:
+        """Batched forward_bidirectional from host memory. `seqs` is a list of int token arrays
+        (or a padded int32 [B, Lmax] array with `out['lengths']`). Returns padded outputs."""
+        if isinstance(seqs, np.ndarray) and seqs.ndim == 2:
+            tokens = np.ascontiguousarray(seqs, dtype=np.int32)
+            lengths = np.ascontiguousarray(out["lengths"], dtype=np.int32)
+        else:
+            lengths = np.array([len(s) for s in seqs], dtype=np.int32)
+            tokens = np.zeros((len(seqs), int(lengths.max())), dtype=np.int32)
+            for i, s in enumerate(seqs):
+                tokens[i, : len(s)] = s
+        B, Lmax = tokens.shape
+        cfg = self.cfg
+        logits = np.empty((B, Lmax, cfg.vocab_size), dtype=np.float32)
+        hidden = np.empty((B, Lmax, cfg.dim), dtype=np.float32) if want_hidden else None
+        contacts = np.empty((B, max(Lmax - 2, 0), max(Lmax - 2, 0)), dtype=np.float32) if want_contacts else None
+        self._chk(lib().esm_forward(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits), _p(hidden),
+                                    _p(contacts)), "esm_forward")
+        res = {"logits": logits, "lengths": lengths}
+        if want_hidden:
+            res["hidden"] = hidden
+        if want_contacts:
+            res["contacts"] = contacts
+        return res
+
+    def forward_device(self, d_tokens, cu_seqlens, d_logits, d_hidden=None, d_contacts=None, d_layer_hidden=None,
+                       stream=None, sync: bool = False) -> None:
+        """Packed forward on device buffers (torch CUDA tensors or raw pointers)."""
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+
+        def ptr(t):
+            if t is None:
+                return None
+            return ctypes.c_void_p(t if isinstance(t, int) else t.data_ptr())
+        s = None if stream is None else ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+        self._chk(lib().esm_forward_device(self._ctx, ptr(d_tokens), _p(cu), cu.size - 1, ptr(d_logits),
+                                           ptr(d_hidden), ptr(d_contacts), ptr(d_layer_hidden), s, int(sync)),
+                  "esm_forward_device")
+
+    def matmul_tiled(self, dtype: int, x, w, bias, in_dim: int, out_dim: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        seq_len = x.size // in_dim
+        w = np.ascontiguousarray(w)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        out = np.empty((seq_len, out_dim), dtype=np.float32)
+        self._chk(lib().esm_matmul_tiled(self._ctx, dtype, _p(x), _p(w), _p(b), in_dim, out_dim, seq_len, _p(out)),
+                  "esm_matmul_tiled")
+        return out
+
+    def check_device(self) -> None:
+        self._chk(lib().esm_check_device(self._ctx), "esm_check_device")

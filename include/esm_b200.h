@@ -1,0 +1,149 @@
+/*
+ * esm_b200.h - C ABI of the B200 (sm_100a) ESM-2 bidirectional encoder forward.
+ *
+ * Drop-in for the hot path of codon-infer v1.12.0 (Rust crate, src/lib.rs): the
+ * forward_bidirectional* family, its weight formats and its outputs. Plain C types only, so the
+ * Rust host binds it with an `extern "C"` block. Every function returns an
+ * ESM_* status code and never aborts; esm_last_error() gives the message of the last failure on a
+ * context.
+ *
+ * Threading: one context per GPU. Calls on one context are serialised by an internal mutex;
+ * contexts on different devices may be driven concurrently from different host threads.
+ */
+#ifndef ESM_B200_H_
+#define ESM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (replace io::Result errors and assert!/index panics of the reference). */
+enum {
+  ESM_OK = 0,
+  ESM_EINVAL = 1,    /* bad argument (null pointer, bad shape, unknown arch)             */
+  ESM_EFORMAT = 2,   /* weight file/blob does not match the declared format (InvalidData) */
+  ESM_ECAPACITY = 3, /* request exceeds the reserved workspace (reference: assert! panic)  */
+  ESM_ECUDA = 4,     /* CUDA runtime error                                                 */
+  ESM_ENCCL = 5,     /* reserved for collective failures                                   */
+  ESM_ETIMEOUT = 6,  /* a device-side bounded wait gave up; the context stays usable       */
+  ESM_ENOMEM = 7,    /* device or host allocation failed                                   */
+  ESM_EIO = 8        /* file could not be opened/read (io::ErrorKind::NotFound, UnexpectedEof) */
+};
+
+/* Weight storage types: CODQ dtype ids, src/lib.rs:874-876. */
+enum { ESM_DTYPE_FP32 = 0, ESM_DTYPE_Q8_0 = 1, ESM_DTYPE_Q4_0 = 2 };
+
+/* Architecture ids: CODQ arch ids, src/lib.rs:879-883. */
+enum { ESM_ARCH_8M = 0, ESM_ARCH_35M = 1, ESM_ARCH_150M = 2, ESM_ARCH_650M = 3, ESM_ARCH_3B = 4 };
+
+/* EsmConfig, src/lib.rs:76-84. */
+typedef struct esm_config {
+  int32_t dim;
+  int32_t hidden_dim;
+  int32_t n_layers;
+  int32_t n_heads;
+  int32_t vocab_size;
+  int32_t max_seq_len;
+  int32_t arch;
+} esm_config;
+
+typedef struct esm_ctx esm_ctx;
+
+/* Number of tensors in the EsmWeights field order (src/lib.rs:299-307), which is also the
+ * grouped_canonical_v1 / CODQ file order (src/lib.rs:369-389, 1175-1193):
+ *  0 tok_emb  1 ln1_w  2 ln1_b  3 wq  4 bq  5 wk  6 bk  7 wv  8 bv  9 wo  10 bo
+ * 11 ln2_w 12 ln2_b 13 fc1_w 14 fc1_b 15 fc2_w 16 fc2_b 17 lnf_w 18 lnf_b 19 classifier
+ * Matrices are row-major [out, in] (src/lib.rs:2629-2634); for Q8_0/Q4_0 they are arrays of
+ * BlockQ8_0 (36 B) / BlockQ4_0 (20 B) along `in`. tok_emb is Q8_0 blocks for Q8_0 models and
+ * FP32 otherwise (src/lib.rs:744-746, docs/Q4_0_SPEC.md:88-92). */
+#define ESM_NUM_TENSORS 20
+
+/* ---- configuration ------------------------------------------------------------------------ */
+
+/* EsmConfig::esm2_8m() .. esm2_3b(), src/lib.rs:87-150. */
+int esm_config_preset(int32_t arch, esm_config* out);
+
+/* EsmConfig::detect_from_file, src/lib.rs:277-297: CODQ header if present, otherwise the file
+ * length table of detect_from_file_len (src/lib.rs:228-275). *dtype receives the storage type
+ * (FP32 for header-less files). */
+int esm_config_detect_file(const char* path, esm_config* out, int32_t* dtype);
+
+/* ---- quantizers (bit-exact with the reference) ---------------------------------------------- */
+
+/* quantize_slice_to_q8 / BlockQ8_0::quantize, src/lib.rs:648-673: n % 32 == 0,
+ * dst holds n/32 blocks of 36 bytes. */
+int esm_quantize_q8(const float* src, int64_t n, void* dst);
+/* quantize_slice_to_q4 / BlockQ4_0::quantize, src/lib.rs:1054-1088: dst holds n/32 x 20 bytes. */
+int esm_quantize_q4(const float* src, int64_t n, void* dst);
+
+/* Tokenizer::encode, src/lib.rs:6511-6521: <cls> + ids + <eos>; returns ESM_ECAPACITY if the
+ * sequence needs more than `cap` tokens. *n_out receives the token count. */
+int esm_tokenize(const char* seq, int32_t* out, int32_t cap, int32_t* n_out);
+
+/* ---- context ------------------------------------------------------------------------------ */
+
+int esm_ctx_create(int32_t device, esm_ctx** out);
+int esm_ctx_destroy(esm_ctx* ctx);
+const char* esm_last_error(const esm_ctx* ctx);
+
+/* EsmWeights{,Q8,Q4}::from_file, src/lib.rs:310-547, 744-830, 1156-1242. `cfg` may be NULL to
+ * autodetect (EsmWeights*::load_from_file). Uploads to the context's device. */
+int esm_load_file(esm_ctx* ctx, const char* path, const esm_config* cfg);
+
+/* Upload weights from host memory: tensors[i] / sizes[i] (bytes) in the order above. */
+int esm_load_host(esm_ctx* ctx, const esm_config* cfg, int32_t dtype, const void* const* tensors,
+                  const size_t* sizes);
+
+/* Contact regression head (EsmConfig::contact_head_weights, src/lib.rs:154-177): w has
+ * n_layers * n_heads entries (layer-major), b is the bias. Required before contacts are asked for. */
+int esm_set_contact_head(esm_ctx* ctx, const float* w, int32_t nw, float b);
+
+/* Workspace for up to `max_tokens` packed tokens in up to `max_seqs` sequences of at most
+ * `max_len` tokens, with room for contact maps when `contacts` != 0 (BidirectionalRunState::new,
+ * src/lib.rs:2510-2544). Calls that exceed it fail with ESM_ECAPACITY. */
+int esm_reserve(esm_ctx* ctx, int32_t max_tokens, int32_t max_seqs, int32_t max_len, int32_t contacts);
+
+/* ---- forward ------------------------------------------------------------------------------- */
+
+/* Batched forward_bidirectional{_parallel,_q8,_q4} (src/lib.rs:5078-5095, 5442-5448, 5790-5798)
+ * from HOST buffers. tokens: [B, Lmax] right-padded; lengths[b] tokens of row b are real (each
+ * sequence is computed exactly as if run alone - key-padding mask). Outputs (host):
+ *   logits   [B, Lmax, vocab]   (state.logits)                        required
+ *   hidden   [B, Lmax, dim]     (state.x = LN_f(x) after the call)     or NULL
+ *   contacts [B, Lmax-2, Lmax-2] sigmoid contact map, row-major over each sequence's own
+ *            n = lengths[b]-2 rows/cols at the top-left (state.contact_probs)  or NULL
+ * Padding positions of the outputs are set to 0. */
+int esm_forward(esm_ctx* ctx, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax,
+                float* logits, float* hidden, float* contacts);
+
+/* Same forward on DEVICE buffers of the context's GPU, packed (varlen) layout:
+ *   d_tokens [T] with T = sum of lengths; h_cu_seqlens [B+1] host prefix sums of the lengths.
+ *   d_logits [T, vocab]; d_hidden [T, dim] or NULL; d_contacts packed per sequence (n_b*n_b
+ *   floats each, n_b = len_b - 2, in sequence order) or NULL;
+ *   d_layer_hidden [n_layers, T, dim] residual stream after each layer (the on_layer hook of
+ *   forward_bidirectional_parallel_ext, src/lib.rs:5097-5103) or NULL.
+ * Enqueued on `stream` (a cudaStream_t, NULL = the context's stream); returns after enqueueing
+ * unless `sync` != 0. */
+int esm_forward_device(esm_ctx* ctx, const int32_t* d_tokens, const int32_t* h_cu_seqlens, int32_t B,
+                       float* d_logits, float* d_hidden, float* d_contacts, float* d_layer_hidden,
+                       void* stream, int32_t sync);
+
+/* matmul_tiled_{fp32,q8,q4}_parallel (src/lib.rs:4803-4827, 4870-4894, 4937-4961) on the GPU, from
+ * HOST buffers: out[p, i] = sum_k W[i, k] * x[p, k] + bias[i] for p < seq_len, i < out_dim.
+ * w is FP32 [out_dim, in_dim] or rows of BlockQ8_0 / BlockQ4_0 (dtype); x is FP32 [seq_len, in_dim];
+ * bias [out_dim] or NULL (zero). Weights are dequantized (q*d) and both operands rounded to fp16
+ * for the tensor cores; accumulation is fp32. in_dim must be a multiple of 32. */
+int esm_matmul_tiled(esm_ctx* ctx, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,
+                     int32_t out_dim, int32_t seq_len, float* out);
+
+/* Device error word check: ESM_ETIMEOUT if a kernel's bounded wait gave up since the last call. */
+int esm_check_device(esm_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ESM_B200_H_ */
