@@ -92,6 +92,16 @@ struct esm_ctx {
   cudaEvent_t plan_ev = nullptr;
   std::vector<int32_t> plan_key;
   int plan_work = 0, plan_tiles = 0;
+  // instrumentation: CUDA event pairs around each launch while profiling is on
+  struct ProfRec {
+    cudaEvent_t a, b;
+    int kind;
+    double flops, bytes;
+  };
+  bool prof = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<ProfRec> prof_recs;
   // host-API staging (grows on demand)
   int32_t* d_padded_tokens = nullptr;
   size_t padded_tok_cap = 0;
@@ -431,6 +441,35 @@ int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, int bn, int e
   return ESM_OK;
 }
 
+cudaEvent_t prof_event(esm_ctx* c) {
+  if (c->ev_used == c->ev_pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    c->ev_pool.push_back(e);
+  }
+  return c->ev_pool[c->ev_used++];
+}
+
+// Brackets one launch with events when profiling is on (no cost otherwise).
+struct ProfScope {
+  esm_ctx* c;
+  cudaStream_t s;
+  int kind;
+  double flops, bytes;
+  cudaEvent_t a = nullptr;
+  ProfScope(esm_ctx* c_, cudaStream_t s_, int kind_, double flops_, double bytes_)
+      : c(c_), s(s_), kind(kind_), flops(flops_), bytes(bytes_) {
+    if (c->prof && (a = prof_event(c))) cudaEventRecord(a, s);
+  }
+  ~ProfScope() {
+    if (!a) return;
+    cudaEvent_t b = prof_event(c);
+    if (!b) return;
+    cudaEventRecord(b, s);
+    c->prof_recs.push_back({a, b, kind, flops, bytes});
+  }
+};
+
 // The forward over packed device tokens. Caller holds the context lock and validated shapes.
 int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B, float* d_logits, float* d_hidden,
                  float* d_contacts, float* d_layer_hidden, cudaStream_t s) {
@@ -455,8 +494,14 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   const int64_t mat_b = esm::matrix_bytes(c->dtype, dd), fc_b = esm::matrix_bytes(c->dtype, fd);
 
   ESM_CUDA(esm::launch_seq_setup(d_tokens, c->cu, B, c->pos, c->seq_of, c->escale, s));
+  const double rowb = static_cast<double>(T) * d;
+  {
+  ProfScope ps(c, s, ESM_PROF_NORM, 0.0, rowb * 6.0);
   ESM_CUDA(esm::launch_embed_ln(d_tokens, c->seq_of, c->escale, c->dtype == ESM_DTYPE_Q8_0 ? nullptr : c->emb_f32,
                                 c->w[0], T, d, ln1_w, ln1_b, c->x, c->xn, s));
+  }
+  int64_t attn_pairs = 0;
+  for (int b = 0; b < B; ++b) attn_pairs += static_cast<int64_t>(h_cu[b + 1] - h_cu[b]) * (h_cu[b + 1] - h_cu[b]);
   int64_t m_total = 0, r_total = 0;
   if (contacts) {
     for (int b = 0; b < B; ++b) {
@@ -492,13 +537,26 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     src.w[5] = static_cast<const uint8_t*>(c->w[15]) + l * fc_b;
     src.elems[0] = src.elems[1] = src.elems[2] = src.elems[3] = dd;
     src.elems[4] = src.elems[5] = fd;
-    ESM_CUDA(esm::launch_dequant_layer(src, c->wqkv16, c->wo16, c->w116, c->w216, s));
-    if (l > 0) ESM_CUDA(esm::launch_layernorm(c->x, T, d, ln1_w + l * d, ln1_b + l * d, c->xn, d, nullptr, s));
-    rc = gemm(c, c->tm_xn, c->tm_wqkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d, c->bqkv + static_cast<int64_t>(l) * 3 * d,
-              c->qkv, 3 * d, s);
-    if (rc) return rc;
-    ESM_CUDA(esm::launch_attention(ap, s));
+    {
+      ProfScope ps(c, s, ESM_PROF_DEQUANT, 0.0, static_cast<double>(4 * mat_b + 2 * fc_b) + 2.0 * (4 * dd + 2 * fd));
+      ESM_CUDA(esm::launch_dequant_layer(src, c->wqkv16, c->wo16, c->w116, c->w216, s));
+    }
+    if (l > 0) {
+      ProfScope ps(c, s, ESM_PROF_NORM, 0.0, rowb * 6.0);
+      ESM_CUDA(esm::launch_layernorm(c->x, T, d, ln1_w + l * d, ln1_b + l * d, c->xn, d, nullptr, s));
+    }
+    {
+      ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * 3.0 * d * d, 0.0);
+      rc = gemm(c, c->tm_xn, c->tm_wqkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d,
+                c->bqkv + static_cast<int64_t>(l) * 3 * d, c->qkv, 3 * d, s);
+      if (rc) return rc;
+    }
+    {
+      ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
+      ESM_CUDA(esm::launch_attention(ap, s));
+    }
     if (contacts) {
+      ProfScope ps(c, s, ESM_PROF_CONTACT, 2.0 * static_cast<double>(attn_pairs) * d, 0.0);
       esm::ContactParams cp{};
       cp.qkv = c->qkv;
       cp.lse = c->lse;
@@ -518,15 +576,27 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       cp.head_base = l * H;
       ESM_CUDA(esm::launch_contact_accumulate(cp, s));
     }
-    rc = gemm(c, c->tm_ao, c->tm_wo, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d, s);
-    if (rc) return rc;
-    ESM_CUDA(esm::launch_layernorm(c->x, T, d, ln2_w + l * d, ln2_b + l * d, c->xn, d, nullptr, s));
-    rc = gemm(c, c->tm_xn, c->tm_w1, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb, F,
-              s);
-    if (rc) return rc;
-    rc = gemm(c, c->tm_hb, c->tm_w2, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x, d,
-              s);
-    if (rc) return rc;
+    {
+      ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(dd), 0.0);
+      rc = gemm(c, c->tm_ao, c->tm_wo, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d, s);
+      if (rc) return rc;
+    }
+    {
+      ProfScope ps(c, s, ESM_PROF_NORM, 0.0, rowb * 6.0);
+      ESM_CUDA(esm::launch_layernorm(c->x, T, d, ln2_w + l * d, ln2_b + l * d, c->xn, d, nullptr, s));
+    }
+    {
+      ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(fd), 0.0);
+      rc = gemm(c, c->tm_xn, c->tm_w1, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb,
+                F, s);
+      if (rc) return rc;
+    }
+    {
+      ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(fd), 0.0);
+      rc = gemm(c, c->tm_hb, c->tm_w2, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x,
+                d, s);
+      if (rc) return rc;
+    }
     if (d_layer_hidden)
       ESM_CUDA(cudaMemcpyAsync(d_layer_hidden + static_cast<int64_t>(l) * T * d, c->x, static_cast<size_t>(T) * d * 4,
                                cudaMemcpyDeviceToDevice, s));
@@ -535,13 +605,17 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   if (contacts) {
     int max_n = 0;
     for (int b = 0; b < B; ++b) max_n = std::max(max_n, h_cu[b + 1] - h_cu[b] - 2);
+    ProfScope ps(c, s, ESM_PROF_CONTACT, 0.0, 0.0);
     ESM_CUDA(esm::launch_contact_finalize(c->M, c->r, c->m_off, c->r_off, c->cu, B, max_n, nl * H, c->d_ch_w, c->ch_b,
                                           c->a_scr, d_contacts, s));
   }
 
   // Final LayerNorm (state.x after the call), then the LM head (src/lib.rs:5379-5439).
   float* hid32 = d_hidden ? d_hidden : (c->has_head ? nullptr : c->hidden);
-  ESM_CUDA(esm::launch_layernorm(c->x, T, d, lnf_w, lnf_b, c->xn, d, hid32, s));
+  {
+    ProfScope ps(c, s, ESM_PROF_NORM, 0.0, rowb * 6.0);
+    ESM_CUDA(esm::launch_layernorm(c->x, T, d, lnf_w, lnf_b, c->xn, d, hid32, s));
+  }
   if (c->has_head) {
     const float* cls = static_cast<const float*>(c->w[19]);
     const float* lm_ln_w = cls;
@@ -549,11 +623,16 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     const float* dense_b = cls + 2 * d + dd;
     const float* dec_w = cls + 3 * d + dd;
     const float* dec_b = dec_w + static_cast<int64_t>(V) * d;
-    rc = gemm(c, c->tm_xn, c->tm_dense, c->bn_dense, esm::kEpiGeluF32, T, d, d, dense_b, c->headf, d, s);
-    if (rc) return rc;
+    {
+      ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(dd), 0.0);
+      rc = gemm(c, c->tm_xn, c->tm_dense, c->bn_dense, esm::kEpiGeluF32, T, d, d, dense_b, c->headf, d, s);
+      if (rc) return rc;
+    }
+    ProfScope ps(c, s, ESM_PROF_HEAD, 2.0 * T * static_cast<double>(V) * d, rowb * 4.0);
     ESM_CUDA(esm::launch_lm_decoder(c->headf, T, d, 1, lm_ln_w, lm_ln_b, dec_w, dec_b, V, d_logits, s));
   } else {
     // Tied-embedding fallback: logits = x E^T with zero bias (src/lib.rs:5429-5439).
+    ProfScope ps(c, s, ESM_PROF_HEAD, 2.0 * T * static_cast<double>(V) * d, rowb * 4.0);
     ESM_CUDA(esm::launch_lm_decoder(hid32, T, d, 0, nullptr, nullptr, c->emb_f32, nullptr, V, d_logits, s));
   }
   return ESM_OK;
@@ -675,6 +754,7 @@ int esm_ctx_destroy(esm_ctx* c) {
     if (c->d_padded_tokens) cudaFree(c->d_padded_tokens);
     if (c->d_padded_out) cudaFree(c->d_padded_out);
     if (c->plan_ev) cudaEventDestroy(c->plan_ev);
+    for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->d_err) cudaFree(c->d_err);
     cudaStreamDestroy(c->stream);
   }
@@ -970,6 +1050,39 @@ int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, c
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return done(fail(c, ESM_ECUDA, std::string("matmul_tiled: ") + cudaGetErrorString(e)));
   return done(check_device_word(c));
+}
+
+int esm_profile_enable(esm_ctx* c, int32_t enable) {
+  if (!c) return ESM_EINVAL;
+  std::lock_guard<std::mutex> lk(c->mu);
+  ESM_CUDA(cudaSetDevice(c->device));
+  ESM_CUDA(cudaDeviceSynchronize());
+  c->prof = enable != 0;
+  c->prof_recs.clear();
+  c->ev_used = 0;
+  return ESM_OK;
+}
+
+int esm_profile_read(esm_ctx* c, int32_t kind, double* total_ms, int64_t* launches, double* flops, double* bytes) {
+  if (!c || kind < 0 || kind >= ESM_PROF_KINDS) return fail(c, ESM_EINVAL, "bad profile kind");
+  std::lock_guard<std::mutex> lk(c->mu);
+  double ms = 0.0, fl = 0.0, by = 0.0;
+  int64_t n = 0;
+  for (const auto& r : c->prof_recs) {
+    if (r.kind != kind) continue;
+    ESM_CUDA(cudaEventSynchronize(r.b));
+    float t = 0.0f;
+    ESM_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+    ms += t;
+    fl += r.flops;
+    by += r.bytes;
+    ++n;
+  }
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = n;
+  if (flops) *flops = fl;
+  if (bytes) *bytes = by;
+  return ESM_OK;
 }
 
 int esm_check_device(esm_ctx* c) {

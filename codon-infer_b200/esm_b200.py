@@ -29,6 +29,7 @@ TENSOR_NAMES = (
     "ln2_w", "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "lnf_w", "lnf_b", "classifier",
 )
 MATRICES = ("wq", "wk", "wv", "wo", "fc1_w", "fc2_w")
+PROFILE_KINDS = ("dequant", "norm", "gemm", "attention", "contact", "head")
 
 
 class EsmError(RuntimeError):
@@ -106,6 +107,8 @@ def lib() -> ctypes.CDLL:
             "esm_forward_device": [vp, vp, vp, i32, vp, vp, vp, vp, vp, i32],
             "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
             "esm_check_device": [vp],
+            "esm_profile_enable": [vp, i32],
+            "esm_profile_read": [vp, i32, vp, vp, vp, vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -298,12 +301,16 @@ class Model:
     def reserve(self, max_tokens: int, max_seqs: int, max_len: int, contacts: bool = False) -> None:
         self._chk(lib().esm_reserve(self._ctx, max_tokens, max_seqs, max_len, int(contacts)), "esm_reserve")
 
-    def forward(self, seqs, want_hidden: bool = False, want_contacts: bool = False, out=None) -> dict:
-        """Batched forward_bidirectional from host memory. `seqs` is a list of int token arrays
-        (or a padded int32 [B, Lmax] array with `out['lengths']`). Returns padded outputs."""
+    def forward(self, seqs, lengths=None, want_hidden: bool = False, want_contacts: bool = False,
+                logits_out: np.ndarray | None = None) -> dict:
+        """Batched forward_bidirectional from host memory.
+
+        `seqs` is a list of int token arrays, or a right-padded int32 [B, Lmax] array together with
+        `lengths`. `logits_out` may be a preallocated (e.g. pinned) float32 [B, Lmax, vocab] array.
+        Returns padded outputs; padding positions are zero."""
         if isinstance(seqs, np.ndarray) and seqs.ndim == 2:
             tokens = np.ascontiguousarray(seqs, dtype=np.int32)
-            lengths = np.ascontiguousarray(out["lengths"], dtype=np.int32)
+            lengths = np.ascontiguousarray(lengths, dtype=np.int32)
         else:
             lengths = np.array([len(s) for s in seqs], dtype=np.int32)
             tokens = np.zeros((len(seqs), int(lengths.max())), dtype=np.int32)
@@ -311,12 +318,15 @@ class Model:
                 tokens[i, : len(s)] = s
         B, Lmax = tokens.shape
         cfg = self.cfg
-        logits = np.empty((B, Lmax, cfg.vocab_size), dtype=np.float32)
+        if logits_out is None:
+            logits_out = np.empty((B, Lmax, cfg.vocab_size), dtype=np.float32)
+        assert logits_out.shape == (B, Lmax, cfg.vocab_size) and logits_out.dtype == np.float32
+        assert logits_out.flags.c_contiguous
         hidden = np.empty((B, Lmax, cfg.dim), dtype=np.float32) if want_hidden else None
         contacts = np.empty((B, max(Lmax - 2, 0), max(Lmax - 2, 0)), dtype=np.float32) if want_contacts else None
-        self._chk(lib().esm_forward(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits), _p(hidden),
+        self._chk(lib().esm_forward(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits_out), _p(hidden),
                                     _p(contacts)), "esm_forward")
-        res = {"logits": logits, "lengths": lengths}
+        res = {"logits": logits_out, "lengths": lengths}
         if want_hidden:
             res["hidden"] = hidden
         if want_contacts:
@@ -345,6 +355,19 @@ class Model:
         out = np.empty((seq_len, out_dim), dtype=np.float32)
         self._chk(lib().esm_matmul_tiled(self._ctx, dtype, _p(x), _p(w), _p(b), in_dim, out_dim, seq_len, _p(out)),
                   "esm_matmul_tiled")
+        return out
+
+    def profile_enable(self, on: bool = True) -> None:
+        self._chk(lib().esm_profile_enable(self._ctx, int(on)), "esm_profile_enable")
+
+    def profile_read(self) -> dict:
+        """Per kernel class: total ms, launches, algorithmic FLOPs and bytes since profile_enable."""
+        out = {}
+        for k, name in enumerate(PROFILE_KINDS):
+            ms, n, fl, by = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_double()
+            self._chk(lib().esm_profile_read(self._ctx, k, ctypes.byref(ms), ctypes.byref(n), ctypes.byref(fl),
+                                             ctypes.byref(by)), "esm_profile_read")
+            out[name] = {"ms": ms.value, "launches": n.value, "flops": fl.value, "bytes": by.value}
         return out
 
     def check_device(self) -> None:

@@ -139,6 +139,25 @@ int esm_forward_device(esm_ctx* ctx, const int32_t* d_tokens, const int32_t* h_c
 int esm_matmul_tiled(esm_ctx* ctx, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,
                      int32_t out_dim, int32_t seq_len, float* out);
 
+/* ---- instrumentation (no counterpart in the reference, which only times whole calls) ---------- */
+
+/* Kernel classes reported by esm_profile_read. */
+enum {
+  ESM_PROF_DEQUANT = 0,   /* per-layer weight dequantization to fp16                 */
+  ESM_PROF_NORM = 1,      /* embedding + LayerNorms                                  */
+  ESM_PROF_GEMM = 2,      /* tcgen05 projection GEMMs (QKV, O, fc1, fc2, LM dense)   */
+  ESM_PROF_ATTENTION = 3, /* attention                                               */
+  ESM_PROF_CONTACT = 4,   /* contact-mode accumulation and APC finalize              */
+  ESM_PROF_HEAD = 5,      /* LM-head LayerNorm + decoder                             */
+  ESM_PROF_KINDS = 6
+};
+
+/* enable != 0: every kernel launched by later forwards is bracketed by CUDA events on its own
+ * stream and counted per class, with its algorithmic FLOPs and bytes; counters are reset. */
+int esm_profile_enable(esm_ctx* ctx, int32_t enable);
+/* Totals for one class since the last enable (synchronizes with the recorded events). */
+int esm_profile_read(esm_ctx* ctx, int32_t kind, double* total_ms, int64_t* launches, double* flops, double* bytes);
+
 /* Device error word check: ESM_ETIMEOUT if a kernel's bounded wait gave up since the last call. */
 int esm_check_device(esm_ctx* ctx);
 

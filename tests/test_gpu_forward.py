@@ -1,0 +1,178 @@
+"""GPU parity of the full encoder forward (C ABI esm_forward / esm_forward_device) against the CPU
+oracle's restatement of forward_bidirectional{_parallel,_q8,_q4} on the same seeded weights and
+sequences, one config per ESM-2 family member of the benchmark set.
+
+Tolerances (stated by the hot-path specification): logits max-abs error <= 2e-2 with >= 99.9 %
+top-1 agreement; contact probabilities max-abs <= 1e-2. Each sequence of a padded batch is
+compared with the oracle run on that sequence alone (the key-padding mask contract).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+TOP1_MIN = 0.999
+CONTACT_TOL = 1e-2
+
+
+def build(esm, cfg, dtype, seed=0, contact=True, bias_std=0.02, ln_jitter=0.1, with_classifier=True):
+    t32 = esm.synth_fp32_tensors(cfg, seed=seed, bias_std=bias_std, ln_jitter=ln_jitter,
+                                 with_classifier=with_classifier)
+    t = esm.quantize_tensors(t32, dtype)
+    m = esm.Model(0)
+    m.load_tensors(cfg, dtype, t)
+    cw = None
+    if contact:
+        rng = np.random.default_rng(seed + 100)
+        cw = (rng.standard_normal(cfg.n_layers * cfg.n_heads) * 0.1).astype(np.float32)
+        cw[::3] = 0.0  # heads with a zero weight are skipped, as in the reference
+        m.set_contact_head(cw, -0.5)
+    return m, t, cw
+
+
+def compare(orc, cfg, dtype, t, seqs, out, cw=None, cb=-0.5):
+    top_ok = top_n = 0
+    for i, s in enumerate(seqs):
+        L = len(s)
+        ref = orc.forward(cfg, dtype, t, s, contact_w=cw, contact_b=cb, want_hidden=True)
+        got = out["logits"][i, :L]
+        assert np.isfinite(got).all()
+        err = np.abs(got - ref["logits"]).max()
+        assert err <= LOGIT_TOL, f"seq {i}: logits max-abs {err:.3e}"
+        top_ok += int((got.argmax(1) == ref["logits"].argmax(1)).sum())
+        top_n += L
+        if "hidden" in out:
+            herr = np.abs(out["hidden"][i, :L] - ref["hidden"]).max()
+            assert herr <= 5e-2, f"seq {i}: hidden max-abs {herr:.3e}"
+        if cw is not None and L > 2:
+            cerr = np.abs(out["contacts"][i, :L - 2, :L - 2] - ref["contacts"]).max()
+            assert cerr <= CONTACT_TOL, f"seq {i}: contacts max-abs {cerr:.3e}"
+        # Padding positions are zero.
+        assert (out["logits"][i, L:] == 0).all()
+    assert top_ok / top_n >= TOP1_MIN, f"top-1 agreement {top_ok / top_n:.4f}"
+
+
+def test_8m_fp32_single_sequence_with_contacts(esm, orc):
+    # Config 1: ESM-2 8M FP32, one sequence of 126 residues (L = 128), contacts on.
+    cfg = esm.esm2_8m()
+    m, t, cw = build(esm, cfg, esm.DTYPE_FP32)
+    m.reserve(128, 1, 128, contacts=True)
+    seqs = esm.random_sequences(1, 128, seed=0)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_FP32, t, seqs, out, cw)
+
+
+def test_35m_q8_ragged_batch(esm, orc):
+    # Config 2 shape: ESM-2 35M Q8_0, right-padded batch with lengths in [64, 512].
+    cfg = esm.esm2_35m()
+    m, t, _ = build(esm, cfg, esm.DTYPE_Q8_0, contact=False)
+    lens = [64, 511, 200, 333]
+    m.reserve(sum(lens), len(lens), 512)
+    seqs = esm.random_sequences(len(lens), lens, seed=2)
+    out = m.forward(seqs, want_hidden=True)
+    compare(orc, cfg, esm.DTYPE_Q8_0, t, seqs, out)
+
+
+def test_150m_fp32_masked_variants(esm, orc):
+    # Config 3 shape: ESM-2 150M FP32, a 300-residue wild type and single-<mask> variants.
+    cfg = esm.esm2_150m()
+    m, t, _ = build(esm, cfg, esm.DTYPE_FP32, contact=False)
+    wt = esm.random_sequences(1, 302, seed=3)[0]
+    seqs = []
+    for p in (1, 150, 300):
+        v = wt.copy()
+        v[p] = esm.MASK_ID
+        seqs.append(v)
+    m.reserve(302 * 3, 3, 302)
+    out = m.forward(seqs)
+    compare(orc, cfg, esm.DTYPE_FP32, t, seqs, out)
+
+
+def test_650m_q4(esm, orc):
+    # Config 4 model: ESM-2 650M Q4_0 (oracle-sized sequence lengths).
+    cfg = esm.esm2_650m()
+    m, t, _ = build(esm, cfg, esm.DTYPE_Q4_0, contact=False)
+    lens = [128, 97]
+    m.reserve(sum(lens), 2, 128)
+    seqs = esm.random_sequences(2, lens, seed=4)
+    out = m.forward(seqs)
+    compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out)
+
+
+def test_3b_shape_q8_contacts_beyond_1024(esm, orc):
+    # Config 5 shapes (d 2560, 40 heads x 64, FFN 10240, Q8_0) with two layers, one sequence longer
+    # than the reference's 1024-entry APC buffer allows, contacts on.
+    base = esm.esm2_3b()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    m, t, cw = build(esm, cfg, esm.DTYPE_Q8_0)
+    m.reserve(1100, 1, 1100, contacts=True)
+    seqs = esm.random_sequences(1, 1100, seed=5)
+    out = m.forward(seqs, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_Q8_0, t, seqs, out, cw)
+
+
+def test_tied_embedding_fallback_head(esm, orc):
+    # Weights without a classifier use logits = x E^T (src/lib.rs:5429-5439); Q8 dequantizes E.
+    cfg = esm.EsmConfig(320, 1280, 2, 20, arch=0)
+    for dt in (esm.DTYPE_FP32, esm.DTYPE_Q8_0):
+        m, t, _ = build(esm, cfg, dt, contact=False, with_classifier=False)
+        m.reserve(64, 1, 64)
+        seqs = esm.random_sequences(1, 64, seed=6)
+        compare(orc, cfg, dt, t, seqs, m.forward(seqs, want_hidden=True))
+
+
+def test_batch_equals_each_sequence_alone(esm):
+    cfg = esm.esm2_35m()
+    m, t, _ = build(esm, cfg, esm.DTYPE_Q4_0, contact=False)
+    lens = [70, 300, 129]
+    seqs = esm.random_sequences(3, lens, seed=7)
+    m.reserve(sum(lens), 3, 300)
+    batch = m.forward(seqs)["logits"]
+    for i, s in enumerate(seqs):
+        alone = m.forward([s])["logits"][0]
+        assert np.array_equal(batch[i, : len(s)], alone)
+
+
+def test_device_api_layer_states_and_mask_scale(esm, orc):
+    import torch
+    cfg = esm.EsmConfig(320, 1280, 3, 20, arch=0)
+    m, t, _ = build(esm, cfg, esm.DTYPE_Q4_0, contact=False)
+    seqs = esm.random_sequences(2, [40, 90], seed=8)
+    seqs[1][10:30] = esm.MASK_ID  # token-dropout scale depends on each sequence's own mask count
+    cu = np.concatenate([[0], np.cumsum([len(s) for s in seqs])]).astype(np.int32)
+    T = int(cu[-1])
+    m.reserve(T, 2, 90)
+    dev = torch.device("cuda:0")
+    d_tok = torch.from_numpy(np.concatenate(seqs)).to(dev)
+    logits = torch.empty(T, cfg.vocab_size, device=dev)
+    layers = torch.empty(cfg.n_layers, T, cfg.dim, device=dev)
+    m.forward_device(d_tok, cu, logits, d_layer_hidden=layers, sync=True)
+    lg, ls = logits.cpu().numpy(), layers.cpu().numpy()
+    for i, s in enumerate(seqs):
+        states = []
+        ref = orc.forward(cfg, esm.DTYPE_Q4_0, t, s, on_layer=lambda l, x: states.append(x))
+        a, b = cu[i], cu[i + 1]
+        assert np.abs(lg[a:b] - ref["logits"]).max() <= LOGIT_TOL
+        for l in range(cfg.n_layers):
+            scale = np.abs(states[l]).max()
+            assert np.abs(ls[l, a:b] - states[l]).max() <= 1e-2 * max(scale, 1.0)
+
+
+def test_capacity_and_argument_errors(esm):
+    cfg = esm.EsmConfig(320, 1280, 1, 20, arch=0)
+    m, _, _ = build(esm, cfg, esm.DTYPE_FP32, contact=False)
+    m.reserve(100, 2, 50)
+    with pytest.raises(esm.EsmError) as e:
+        m.forward(esm.random_sequences(1, 60))
+    assert e.value.code == esm.ESM_ECAPACITY
+    with pytest.raises(esm.EsmError) as e:
+        m.forward(esm.random_sequences(1, 40), want_contacts=True)
+    assert e.value.code == esm.ESM_ECAPACITY
+    with pytest.raises(esm.EsmError) as e:
+        m.set_contact_head(np.zeros(3, np.float32), 0.0)
+    assert e.value.code == esm.ESM_EINVAL
+    # The context stays usable after rejected calls.
+    out = m.forward(esm.random_sequences(2, 50))
+    assert np.isfinite(out["logits"]).all()
+    m.check_device()
