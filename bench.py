@@ -172,6 +172,8 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
     arch, dtype, batch, seq_len = CONFIGS[args.config]
+    if args.batch:
+        batch = args.batch  # smaller per-GPU batch for profiler captures only
     cfg = esm.EsmConfig.preset(arch)
     t32 = esm.synth_fp32_tensors(cfg, seed=0)
     tensors = esm.quantize_tensors(t32, dtype)
@@ -319,6 +321,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
