@@ -139,6 +139,23 @@ int esm_forward_device(esm_ctx* ctx, const int32_t* d_tokens, const int32_t* h_c
 int esm_matmul_tiled(esm_ctx* ctx, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,
                      int32_t out_dim, int32_t seq_len, float* out);
 
+/* No counterpart in the reference. The GEMM of esm_matmul_tiled for callers that cannot allocate
+ * device memory (a process whose device memory is all reserved up front by its own allocator, a
+ * latency-critical pipeline that cannot take cudaMalloc's device-wide synchronisation, a plugin
+ * host that forbids allocation). Inputs and output are the caller's DEVICE buffers: d_x fp32
+ * [seq_len, in_dim] and d_out fp32 [seq_len, out_dim] 16-byte aligned, d_w as in esm_matmul_tiled,
+ * d_bias [out_dim] or NULL. Its only scratch is a static device array of ESM_NOALLOC_SCRATCH_BYTES
+ * that holds the fp16 operand copies (2*(seq_len + out_dim)*in_dim bytes, 256-byte aligned each),
+ * the bias padded to a multiple of 16 and, when out_dim % 16 != 0, a padded fp32 output; larger
+ * problems return ESM_ECAPACITY. The array lives on every GPU where the library's device code is
+ * loaded until the process exits. The first call on a device looks up the array's device address
+ * and loads the kernels it uses, so make it before any stream capture. Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. The call is enqueued on
+ * `stream` (a cudaStream_t, NULL = legacy default) and returns once the result is in d_out. */
+#define ESM_NOALLOC_SCRATCH_BYTES (32u << 20)
+int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const void* d_w, const float* d_bias, int32_t in_dim,
+                             int32_t out_dim, int32_t seq_len, float* d_out, void* stream);
+
 /* ---- instrumentation (no counterpart in the reference, which only times whole calls) ---------- */
 
 /* Kernel classes reported by esm_profile_read. */
