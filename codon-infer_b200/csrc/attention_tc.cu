@@ -1,0 +1,305 @@
+// Bidirectional attention on the 5th-generation tensor cores (tcgen05) for head_dim 64, the
+// ESM-2 650M and 3B shape. Same contract as attention_kernel in attention.cu (packed varlen
+// sequences, keys past a sequence's end masked, O in fp16, optional per-row log-sum-exp), which
+// replaces the reference attention loop (src/lib.rs:5206-5301).
+//
+// One CTA per (sequence, 128-query tile, head); 192 threads; two CTAs per SM.
+//   warp 0      TMA producer: Q tile once, then 64-key K and V tiles into a 2-stage ring.
+//   warp 1      tcgen05.mma issuer (one thread): S = Q K^T (M 128, N 64, K 64) into tensor memory,
+//               then O_j = P_j V_j (M 128, N 64, K 64) with V as an MN-major operand.
+//   warps 2..5  softmax, one query row per thread: read S from tensor memory, online max/sum in
+//               fp32, P = exp2(S*scale*log2e - m) rounded to fp16 into shared memory in the
+//               128-byte-swizzled K-major layout the MMA reads, and O accumulated in registers
+//               as O = O*alpha + O_j.
+// Tensor memory: S in columns [0, 64), O_j in [64, 128). All waits are bounded.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace esm {
+
+namespace {
+
+constexpr int kQ = 128;   // query rows per CTA
+constexpr int kKV = 64;   // keys per tile
+constexpr int kD = 64;    // head dim
+constexpr int kThreadsAt = 192;
+constexpr int kQBytes = kQ * kD * 2;    // 16 KiB
+constexpr int kKVBytes = kKV * kD * 2;  // 8 KiB
+constexpr int kPBytes = kQ * kKV * 2;   // 16 KiB
+constexpr int kOffK = kQBytes;
+constexpr int kOffV = kOffK + 2 * kKVBytes;
+constexpr int kOffP = kOffV + 2 * kKVBytes;
+constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kSmemAt = kOffBar + 256 + 1024;
+constexpr uint32_t kTmemCols = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// MN-major operand descriptor, 128-byte swizzle: rows of 128 bytes hold 64 fp16 along N, 8-row
+// groups along K are 1024 bytes apart (SBO). Used for V (keys x head_dim, head_dim contiguous).
+__device__ __forceinline__ uint64_t umma_sdesc_sw128_mn(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;          // leading byte offset: one 64-element atom along N
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset between 8-row K groups
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+__global__ void __launch_bounds__(kThreadsAt, 2)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
+                        const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* o_full = bars + 8;
+  uint64_t* o_free = bars + 9;
+  uint64_t* drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int2 wk = p.work[blockIdx.x];
+  const int b = wk.x, q0 = wk.y * kQ, h = blockIdx.y;
+  const int start = p.cu_seqlens[b];
+  const int len = p.cu_seqlens[b + 1] - start;
+  const int nkv = (len + kKV - 1) / kKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 4);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem;        // S: columns [0, 64)
+  const uint32_t t_o = tmem + 64;   // O_j: columns [64, 128)
+
+  if (warp == 0) {
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_kv);
+      const uint64_t pol = l2_policy_evict_normal();
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      tma_load_2d(smem, &tmap_q, q_full, h * kD, start + q0, pol);
+      bool ok = true;
+      int j = 0;
+      for (; j < nkv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, p.err, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
+        tma_load_2d(smem + kOffK + st * kKVBytes, &tmap_kv, &kv_full[st], p.d + h * kD, start + j * kKV, pol);
+        tma_load_2d(smem + kOffV + st * kKVBytes, &tmap_kv, &kv_full[st], 2 * p.d + h * kD, start + j * kKV, pol);
+      }
+      if (!ok) {
+        mbar_wait(q_full, 0, p.err, kDevTimeoutProducer);
+        for (int jj = (j - 2 > 0 ? j - 2 : 0); jj < j; ++jj)
+          mbar_wait(&kv_full[jj & 1], (jj >> 1) & 1, p.err, kDevTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc_qk = umma_idesc_f16(kQ, kKV);
+      constexpr uint32_t idesc_pv = umma_idesc_f16(kQ, kD) | (1u << 16);  // B (V) is MN-major
+      const uint32_t q_addr = smem_u32(smem);
+      const uint32_t p_addr = smem_u32(smem + kOffP);
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutMma);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_full[st], ph, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + kOffK + st * kKVBytes);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_f16(t_s, umma_sdesc_sw128(q_addr + k * 32), umma_sdesc_sw128(k_addr + k * 32), idesc_qk, k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (j > 0 && !mbar_wait(o_free, (j - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + kOffV + st * kKVBytes);
+#pragma unroll
+        for (int k = 0; k < kKV / 16; ++k)
+          umma_f16(t_o, umma_sdesc_sw128(p_addr + k * 32), umma_sdesc_sw128_mn(v_addr + k * 2048), idesc_pv, k > 0);
+        umma_commit(o_full);
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, p.err, kDevTimeoutMma);
+      }
+    }
+  } else {
+    // ---------------- softmax: thread = query row ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // row inside the tile = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const float c = p.scale * kLog2e;
+    float o[kD];
+#pragma unroll
+    for (int i = 0; i < kD; ++i) o[i] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    uint8_t* prow = smem + kOffP + r * 128;
+    const int sw = r & 7;
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; ++j) {
+      // 1. fold O_{j-1} = P_{j-1} V_{j-1} (scale m_{j-1}) into the register accumulator.
+      if (j > 0) {
+        if (!mbar_wait(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t t[32];
+          tmem_ld32(t_o + lane_off + half * 32, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[half * 32 + i] += __uint_as_float(t[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free);
+      }
+      // 2. scores of tile j.
+      if (!mbar_wait(s_full, j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      float s[kKV];
+      {
+        uint32_t t[32];
+        tmem_ld32(t_s + lane_off, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(t[i]);
+        tmem_ld32(t_s + lane_off + 32, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(t[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);  // the next Q K^T may overwrite S
+      const int kbase = j * kKV;
+      if (kbase + kKV > len) {
+#pragma unroll
+        for (int i = 0; i < kKV; ++i)
+          if (kbase + i >= len) s[i] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < kKV; ++i) mx = fmaxf(mx, s[i]);
+      const float m_new = fmaxf(m, mx);
+      const float ms = m_new * c;
+      const float alpha = exp2f(m * c - ms);  // 0 on the first tile (m = -inf)
+      float rs = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kKV; ++i) {
+        s[i] = exp2f(s[i] * c - ms);
+        rs += s[i];
+      }
+      l = l * alpha + rs;
+      m = m_new;
+#pragma unroll
+      for (int i = 0; i < kD; ++i) o[i] *= alpha;
+      // 3. P_j (fp16) into the swizzled K-major tile: 16-byte chunk k of row r lands at chunk k ^ (r & 7).
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        __half2 hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(s[8 * k + 2 * e], s[8 * k + 2 * e + 1]);
+        *reinterpret_cast<uint4*>(prow + ((k ^ sw) << 4)) = *reinterpret_cast<uint4*>(hv);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_full, (nkv - 1) & 1, p.err, kDevTimeoutEpilogue)) {
+      tc_fence_after();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t t[32];
+        tmem_ld32(t_o + lane_off + half * 32, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[half * 32 + i] += __uint_as_float(t[i]);
+      }
+      const int row = q0 + r;
+      if (row < len) {
+        const float inv = 1.0f / l;
+        __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * kD;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          __half2 hv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(o[8 * k + 2 * e] * inv, o[8 * k + 2 * e + 1] * inv);
+          *reinterpret_cast<uint4*>(dst + 8 * k) = *reinterpret_cast<uint4*>(hv);
+        }
+        if (p.lse) p.lse[static_cast<size_t>(h) * p.T + start + row] = m * p.scale + logf(l);
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
+                                cudaStream_t s) {
+  if (p.n_work <= 0) return cudaSuccess;
+  if (p.dh != kD) return cudaErrorInvalidValue;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !(configured & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAt);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) configured |= (1ull << dev);
+  }
+  dim3 grid(p.n_work, p.H);
+  attention_tc_kernel<<<grid, kThreadsAt, kSmemAt, s>>>(tm_q, tm_kv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace esm

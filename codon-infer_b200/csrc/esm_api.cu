@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <mutex>
@@ -27,6 +28,8 @@ struct esm_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
   int num_sms = 148;
+  int cta_pair = 0;  // GEMM tiles on CTA pairs when ESM_GEMM_CTA_PAIR=1 (single CTAs measured faster)
+  int attn_tc = 1;   // tcgen05 attention for head_dim 64 (ESM_ATTN_TC=0 selects the mma.sync kernel)
   std::mutex mu;
   std::string err;
   int* d_err = nullptr;
@@ -75,6 +78,7 @@ struct esm_ctx {
   int32_t* cu = nullptr;
   float* escale = nullptr;
   int2* work = nullptr;
+  int2* work128 = nullptr;
   int4* ctiles = nullptr;
   int64_t* m_off = nullptr;
   int64_t* r_off = nullptr;
@@ -83,15 +87,17 @@ struct esm_ctx {
   float* a_scr = nullptr;
   float* cmap = nullptr;
   CUtensorMap tm_xn, tm_ao, tm_hb;
+  CUtensorMap tm_qkv_q, tm_qkv_kv;  // qkv [T, 3d] with 64-column boxes of 128 / 64 rows
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
+  int2* h_work128 = nullptr;
   int4* h_tiles = nullptr;
   int64_t* h_moff = nullptr;
   int64_t* h_roff = nullptr;
   cudaEvent_t plan_ev = nullptr;
   std::vector<int32_t> plan_key;
-  int plan_work = 0, plan_tiles = 0;
+  int plan_work = 0, plan_work128 = 0, plan_tiles = 0;
   // instrumentation: CUDA event pairs around each launch while profiling is on
   struct ProfRec {
     cudaEvent_t a, b;
@@ -107,6 +113,9 @@ struct esm_ctx {
   size_t padded_tok_cap = 0;
   float* d_padded_out = nullptr;
   size_t padded_out_cap = 0;
+  // mutational-scan staging (grows on demand): tok_row, wt_tok, deltas, entropy
+  void* d_dms = nullptr;
+  size_t dms_cap = 0;
 };
 
 namespace {
@@ -141,11 +150,12 @@ void free_list(std::vector<void*>& list) {
 }
 
 void free_pinned(esm_ctx* c) {
-  for (void* p : {static_cast<void*>(c->h_cu), static_cast<void*>(c->h_work), static_cast<void*>(c->h_tiles),
-                  static_cast<void*>(c->h_moff), static_cast<void*>(c->h_roff)})
+  for (void* p : {static_cast<void*>(c->h_cu), static_cast<void*>(c->h_work), static_cast<void*>(c->h_work128),
+                  static_cast<void*>(c->h_tiles), static_cast<void*>(c->h_moff), static_cast<void*>(c->h_roff)})
     if (p) cudaFreeHost(p);
   c->h_cu = nullptr;
   c->h_work = nullptr;
+  c->h_work128 = nullptr;
   c->h_tiles = nullptr;
   c->h_moff = nullptr;
   c->h_roff = nullptr;
@@ -188,11 +198,12 @@ int build_weight_maps(esm_ctx* c) {
   c->bn_fc1 = esm::gemm_pick_bn(F, 0);
   c->bn_fc2 = esm::gemm_pick_bn(d, 0);
   c->bn_dense = esm::gemm_pick_bn(d, 0);
-  bool ok = esm::make_tmap_f16(&c->tm_wqkv, c->wqkv16, 3 * d, d, d, c->bn_qkv) &&
-            esm::make_tmap_f16(&c->tm_wo, c->wo16, d, d, d, c->bn_o) &&
-            esm::make_tmap_f16(&c->tm_w1, c->w116, F, d, d, c->bn_fc1) &&
-            esm::make_tmap_f16(&c->tm_w2, c->w216, d, F, F, c->bn_fc2);
-  if (ok && c->has_head) ok = esm::make_tmap_f16(&c->tm_dense, c->dense16, d, d, d, c->bn_dense);
+  // Weight (B operand) maps load half tiles: bn/2 rows per box.
+  bool ok = esm::make_tmap_f16(&c->tm_wqkv, c->wqkv16, 3 * d, d, d, c->bn_qkv / 2) &&
+            esm::make_tmap_f16(&c->tm_wo, c->wo16, d, d, d, c->bn_o / 2) &&
+            esm::make_tmap_f16(&c->tm_w1, c->w116, F, d, d, c->bn_fc1 / 2) &&
+            esm::make_tmap_f16(&c->tm_w2, c->w216, d, F, F, c->bn_fc2 / 2);
+  if (ok && c->has_head) ok = esm::make_tmap_f16(&c->tm_dense, c->dense16, d, d, d, c->bn_dense / 2);
   return ok ? ESM_OK : fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for a weight matrix");
 }
 
@@ -337,6 +348,7 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   A(&c->cu, max_seqs + 1);
   A(&c->escale, max_seqs);
   A(&c->work, c->work_cap);
+  A(&c->work128, c->work_cap);
   A(&c->ctiles, c->tiles_cap);
   A(&c->m_off, max_seqs);
   A(&c->r_off, max_seqs);
@@ -359,12 +371,15 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   }
   ESM_CUDA(cudaMallocHost(&c->h_cu, sizeof(int32_t) * (max_seqs + 1)));
   ESM_CUDA(cudaMallocHost(&c->h_work, sizeof(int2) * c->work_cap));
+  ESM_CUDA(cudaMallocHost(&c->h_work128, sizeof(int2) * c->work_cap));
   ESM_CUDA(cudaMallocHost(&c->h_tiles, sizeof(int4) * c->tiles_cap));
   ESM_CUDA(cudaMallocHost(&c->h_moff, sizeof(int64_t) * max_seqs));
   ESM_CUDA(cudaMallocHost(&c->h_roff, sizeof(int64_t) * max_seqs));
   bool ok = esm::make_tmap_f16(&c->tm_xn, c->xn, rows, d, d, 128) &&
             esm::make_tmap_f16(&c->tm_ao, c->ao, rows, d, d, 128) &&
-            esm::make_tmap_f16(&c->tm_hb, c->hb, rows, F, F, 128);
+            esm::make_tmap_f16(&c->tm_hb, c->hb, rows, F, F, 128) &&
+            esm::make_tmap_f16(&c->tm_qkv_q, c->qkv, rows, 3 * d, 3 * d, 128) &&
+            esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -384,7 +399,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   const int64_t hl = static_cast<int64_t>(g.n_layers) * g.n_heads;
   // The previous plan's copies must have left the pinned staging before it is rewritten.
   if (c->plan_ev) ESM_CUDA(cudaEventSynchronize(c->plan_ev));
-  int nw = 0, nt = 0;
+  int nw = 0, nw128 = 0, nt = 0;
   int64_t moff = 0, roff = 0;
   for (int b = 0; b <= B; ++b) c->h_cu[b] = h_cu[b];
   for (int b = 0; b < B; ++b) {
@@ -392,6 +407,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
     const int qt = (len + 63) / 64;
     if (nw + qt > c->work_cap) return fail(c, ESM_ECAPACITY, "attention work list exceeds the reserved capacity");
     for (int t = 0; t < qt; ++t) c->h_work[nw++] = make_int2(b, t);
+    for (int t = 0; t < (len + 127) / 128; ++t) c->h_work128[nw128++] = make_int2(b, t);
     if (contacts) {
       const int64_t n = std::max(len - 2, 0);
       c->h_moff[b] = moff;
@@ -410,6 +426,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
     return fail(c, ESM_ECAPACITY, "contact maps exceed the reserved capacity");
   ESM_CUDA(cudaMemcpyAsync(c->cu, c->h_cu, sizeof(int32_t) * (B + 1), cudaMemcpyHostToDevice, s));
   ESM_CUDA(cudaMemcpyAsync(c->work, c->h_work, sizeof(int2) * nw, cudaMemcpyHostToDevice, s));
+  ESM_CUDA(cudaMemcpyAsync(c->work128, c->h_work128, sizeof(int2) * nw128, cudaMemcpyHostToDevice, s));
   if (contacts) {
     ESM_CUDA(cudaMemcpyAsync(c->m_off, c->h_moff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
     ESM_CUDA(cudaMemcpyAsync(c->r_off, c->h_roff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
@@ -419,6 +436,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   ESM_CUDA(cudaEventRecord(c->plan_ev, s));
   c->plan_key = key;
   c->plan_work = nw;
+  c->plan_work128 = nw128;
   c->plan_tiles = nt;
   return ESM_OK;
 }
@@ -437,7 +455,7 @@ int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, int bn, int e
   p.rope_cols = 2 * c->cfg.dim;
   p.err = c->d_err;
   const int dh = c->cfg.dim / c->cfg.n_heads;
-  ESM_CUDA(esm::gemm_launch(ta, tb, bn, epi, epi == esm::kEpiQkvRope ? dh : 0, p, c->num_sms, s));
+  ESM_CUDA(esm::gemm_launch(ta, tb, bn, epi, epi == esm::kEpiQkvRope ? dh : 0, p, c->num_sms, s, c->cta_pair));
   return ESM_OK;
 }
 
@@ -525,6 +543,11 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.H = H;
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
+  ap.err = c->d_err;
+  const bool attn_tc = c->attn_tc && dh == 64;
+  esm::AttnParams ap128 = ap;
+  ap128.work = c->work128;
+  ap128.n_work = c->plan_work128;
 
   for (int l = 0; l < nl; ++l) {
     esm::LayerSrc src{};
@@ -553,7 +576,11 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
-      ESM_CUDA(esm::launch_attention(ap, s));
+      if (attn_tc) {
+        ESM_CUDA(esm::launch_attention_tc(c->tm_qkv_q, c->tm_qkv_kv, ap128, s));
+      } else {
+        ESM_CUDA(esm::launch_attention(ap, s));
+      }
     }
     if (contacts) {
       ProfScope ps(c, s, ESM_PROF_CONTACT, 2.0 * static_cast<double>(attn_pairs) * d, 0.0);
@@ -732,6 +759,8 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   esm_ctx* c = new esm_ctx();
   c->device = device;
   c->num_sms = prop.multiProcessorCount;
+  if (const char* v = std::getenv("ESM_GEMM_CTA_PAIR")) c->cta_pair = std::atoi(v) != 0;
+  if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v) != 0;
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
     delete c;
@@ -753,6 +782,7 @@ int esm_ctx_destroy(esm_ctx* c) {
     if (c->d_ch_w) cudaFree(c->d_ch_w);
     if (c->d_padded_tokens) cudaFree(c->d_padded_tokens);
     if (c->d_padded_out) cudaFree(c->d_padded_out);
+    if (c->d_dms) cudaFree(c->d_dms);
     if (c->plan_ev) cudaEventDestroy(c->plan_ev);
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->d_err) cudaFree(c->d_err);
@@ -994,6 +1024,82 @@ int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32
   return check_device_word(c);
 }
 
+int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
+                            float* entropy) {
+  if (!c || !residues || !deltas || !entropy) return fail(c, ESM_EINVAL, "null argument");
+  if (n <= 0) return fail(c, ESM_EINVAL, "Sequence cannot be empty");
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (!c->loaded) return fail(c, ESM_EINVAL, "no weights loaded");
+  if (c->cap_tokens == 0) return fail(c, ESM_EINVAL, "call esm_reserve before the first forward");
+  ESM_CUDA(cudaSetDevice(c->device));
+  cudaStream_t s = c->stream;
+  const int max_len = c->cfg.max_seq_len;
+  // Window arithmetic of run_pipeline_dms_with_mode (src/pipeline.rs:88-94, 111-121).
+  const int actual_window = (n <= window_size || window_size == 0) ? std::min(n, max_len) : std::min(window_size, max_len);
+  const int half_w = actual_window / 2;
+  if (actual_window + 2 > c->cap_len)
+    return fail(c, ESM_ECAPACITY, "window of " + std::to_string(actual_window + 2) + " tokens exceeds max_len " +
+                                      std::to_string(c->cap_len));
+  // Staging: tok_row[n] | wt_tok[n] | deltas[20 n] | entropy[n]
+  const size_t need = static_cast<size_t>(n) * (2 * 4 + 21 * 4);
+  if (need > c->dms_cap) {
+    if (c->d_dms) cudaFree(c->d_dms);
+    c->d_dms = nullptr;
+    c->dms_cap = 0;
+    ESM_CUDA(cudaMalloc(&c->d_dms, need));
+    c->dms_cap = need;
+  }
+  int32_t* d_row = static_cast<int32_t*>(c->d_dms);
+  int32_t* d_wt = d_row + n;
+  float* d_delta = reinterpret_cast<float*>(d_wt + n);
+  float* d_ent = d_delta + static_cast<size_t>(20) * n;
+  std::vector<int32_t> toks, cu{0}, rows, wts;
+  int p0 = 0;
+  for (int p = 0; p <= n; ++p) {
+    const bool flush = (p == n) || static_cast<int>(cu.size()) - 1 == c->cap_seqs ||
+                       cu.back() + actual_window + 2 > c->cap_tokens;
+    if (flush && cu.size() > 1) {
+      // One batch of masked variants through the forward, then score their masked rows.
+      const int B = static_cast<int>(cu.size()) - 1;
+      int rc = validate_call(c, cu.data(), B, false);
+      if (rc) return rc;
+      ESM_CUDA(cudaMemcpyAsync(c->tokens, toks.data(), toks.size() * 4, cudaMemcpyHostToDevice, s));
+      ESM_CUDA(cudaMemcpyAsync(d_row + p0, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, s));
+      ESM_CUDA(cudaMemcpyAsync(d_wt + p0, wts.data(), wts.size() * 4, cudaMemcpyHostToDevice, s));
+      rc = forward_impl(c, c->tokens, cu.data(), B, c->logits, nullptr, nullptr, nullptr, s);
+      if (rc) return rc;
+      ESM_CUDA(esm::launch_dms_score(c->logits, c->cfg.vocab_size, d_row + p0, d_wt + p0, B,
+                                     d_delta + static_cast<size_t>(20) * p0, d_ent + p0, s));
+      // The host vectors are reused by the next batch: wait for this batch's uploads.
+      ESM_CUDA(cudaStreamSynchronize(s));
+      toks.clear();
+      rows.clear();
+      wts.clear();
+      cu.assign(1, 0);
+      p0 = p;
+    }
+    if (p == n) break;
+    int w_start;
+    if (p < half_w) w_start = 0;
+    else if (p + half_w > n) w_start = std::max(n - actual_window, 0);
+    else w_start = p - half_w;
+    const int w_end = std::min(w_start + actual_window, n);
+    const int rel = p - w_start;
+    const int base = cu.back();
+    toks.push_back(0);
+    for (int i = w_start; i < w_end; ++i) toks.push_back(residues[i]);
+    toks.push_back(2);
+    toks[base + rel + 1] = 32;
+    rows.push_back(base + rel + 1);
+    wts.push_back(residues[p]);
+    cu.push_back(base + (w_end - w_start) + 2);
+  }
+  ESM_CUDA(cudaMemcpyAsync(deltas, d_delta, static_cast<size_t>(20) * n * 4, cudaMemcpyDeviceToHost, s));
+  ESM_CUDA(cudaMemcpyAsync(entropy, d_ent, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, s));
+  ESM_CUDA(cudaStreamSynchronize(s));
+  return check_device_word(c);
+}
+
 int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,
                      int32_t out_dim, int32_t seq_len, float* out) {
   if (!c || !x || !w || !out) return fail(c, ESM_EINVAL, "null argument");
@@ -1034,7 +1140,8 @@ int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, c
   if (e == cudaSuccess) e = esm::launch_to_f16(ESM_DTYPE_FP32, x32, static_cast<int64_t>(seq_len) * in_dim, x16, s);
   if (e == cudaSuccess) e = esm::launch_to_f16(dtype, wd, static_cast<int64_t>(out_dim) * in_dim, w16, s);
   if (e != cudaSuccess) return done(fail(c, ESM_ECUDA, std::string("matmul_tiled setup: ") + cudaGetErrorString(e)));
-  if (!esm::make_tmap_f16(&ta, x16, rows, in_dim, in_dim, 128) || !esm::make_tmap_f16(&tb, w16, n_pad, in_dim, in_dim, bn))
+  if (!esm::make_tmap_f16(&ta, x16, rows, in_dim, in_dim, 128) ||
+      !esm::make_tmap_f16(&tb, w16, n_pad, in_dim, in_dim, bn / 2))
     return done(fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed"));
   p.M = seq_len;
   p.N = n_pad;
@@ -1043,7 +1150,7 @@ int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, c
   p.out = o32;
   p.ldo = n_pad;
   p.err = c->d_err;
-  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, c->num_sms, s);
+  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, c->num_sms, s, c->cta_pair);
   if (e == cudaSuccess)
     e = cudaMemcpy2DAsync(out, static_cast<size_t>(out_dim) * 4, o32, static_cast<size_t>(n_pad) * 4,
                           static_cast<size_t>(out_dim) * 4, seq_len, cudaMemcpyDeviceToHost, s);

@@ -6,16 +6,20 @@
 // them on the hot path: apply_rope (src/lib.rs:3533-3552), gelu (3494-3498) and the residual
 // adds (5325-5327, 5364-5366).
 //
-// CTA layout (192 threads, one CTA per SM):
-//   warp 0      TMA producer: stages 128x64 A tiles and BNx64 B tiles (128-byte swizzle) into a
+// CTA layout (320 threads, one CTA per SM):
+//   warp 0      TMA producer: stages 128x64 A tiles and (BN/CG)x64 B tiles (128-byte swizzle) into a
 //               ring of shared-memory stages, completion tracked by mbarrier transaction bytes;
-//   warp 1      allocates tensor memory and issues tcgen05.mma (M=128, N=BN, K=16) from one thread,
-//               releasing each stage with tcgen05.commit;
-//   warps 2..5  epilogue: tcgen05.ld of their 32-lane quarter of the accumulator, fused math,
-//               stores to global memory.
+//   warp 1      allocates tensor memory and issues tcgen05.mma from one thread, releasing each stage
+//               with tcgen05.commit;
+//   warps 2..9  epilogue: two warps per 32-lane quarter of the accumulator (tcgen05.ld only reaches
+//               the quarter given by warp id mod 4), each taking half of the tile's columns.
+// CG = 2 runs the tile on a CTA pair (cluster of 2, tcgen05 cta_group::2): one M = 256 x N = BN MMA
+// per K step, each CTA holding 128 rows of A and BN/2 rows of B, so each SM streams half as many
+// operand bytes per FLOP. The leader CTA issues the MMAs and counts both CTAs' TMA bytes on its
+// barriers; each CTA's epilogue drains its own 128 accumulator rows.
 // Two accumulator buffers in tensor memory let the epilogue of tile i overlap the mainloop of
 // tile i+1. Every wait is bounded (globaltimer), so a broken pipeline reports an error instead of
-// hanging the GPU.
+// hanging the GPU. No load is multicast.
 #include <cstdio>
 
 #include "common.cuh"
@@ -25,23 +29,25 @@ namespace esm {
 
 namespace {
 
-constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle span of fp16
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemBudget = 200 * 1024;
 
-template <int BN>
+template <int BN, int CG>
 struct GemmShape {
-  static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kRows = 128;          // accumulator rows per CTA
+  static constexpr int kBRows = BN / CG;     // B rows staged per CTA
+  static constexpr int kABytes = kRows * kBK * 2;
+  static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
-  static constexpr int kAccStride = BN <= 128 ? 128 : 256;   // TMEM columns between the two accumulators
+  static constexpr int kAccStride = BN <= 128 ? 128 : 256;  // TMEM columns between the two accumulators
   static constexpr int kTmemCols = 2 * kAccStride;
   static constexpr int kBarrierBytes = (2 * kStages + 5) * 8 + 16;
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // +1024 for alignment
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is a multiple of 16 in [16, 256]");
-  static_assert(kBBytes % 1024 == 0, "B tile must keep stages 1024-byte aligned");
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N is a multiple of 16 in [16, 256]");
+  static_assert((BN / 2) % 8 == 0, "B half tiles must keep stages 1024-byte aligned");
   static_assert(kStages >= 2, "need at least two stages");
 };
 
@@ -52,11 +58,82 @@ __device__ __forceinline__ void store_f16x8(__half* dst, const float* v) {
   *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
 }
 
-template <int BN, int EPI, int DH>
+// GELU with the Abramowitz-Stegun erf of the reference, using the fast exp/divide intrinsics
+// (relative error ~1e-6, far below the fp16 rounding of the output).
+__device__ __forceinline__ float gelu_fast(float x) {
+  const float z = x * 0.70710678118654752440f;
+  const float az = fabsf(z);
+  const float t = __fdividef(1.0f, 1.0f + 0.3275911f * az);
+  const float poly = ((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f;
+  float y = 1.0f - poly * t * __expf(-az * az);
+  y = (z < 0.0f) ? -y : y;
+  return 0.5f * x * (1.0f + y);
+}
+
+// Epilogue math and store of 16 consecutive accumulator columns [n, n + 16) of row m.
+template <int EPI>
+__device__ __forceinline__ void epi16(const GemmParams& p, int m, int n, const uint32_t* r) {
+  float v[16];
+  if (p.bias) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 b = __ldg(b4 + i);
+      v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + b.x;
+      v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + b.y;
+      v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + b.z;
+      v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  }
+  if constexpr (EPI == kEpiGeluF16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = gelu_fast(v[i]);
+    __half* dst = static_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + n;
+    store_f16x8(dst, v);
+    store_f16x8(dst + 8, v + 8);
+  } else {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
+    if constexpr (EPI == kEpiGeluF32) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = gelu_fast(v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+}
+
+// Residual update x[m, n..n+16) += acc + bias; the current x values are requested before the
+// tensor-memory load is waited for, so both latencies overlap.
+__device__ __forceinline__ void resid16_load(const GemmParams& p, int m, int n, float4 (&x)[4]) {
+  const float4* src =
+      reinterpret_cast<const float4*>(static_cast<const float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = src[i];
+}
+__device__ __forceinline__ void resid16_store(const GemmParams& p, int m, int n, const uint32_t* r,
+                                              const float4 (&x)[4]) {
+  float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
+  const float4* b4 = reinterpret_cast<const float4*>(p.bias + n);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 b = p.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 o = x[i];
+    o.x += __uint_as_float(r[4 * i + 0]) + b.x;
+    o.y += __uint_as_float(r[4 * i + 1]) + b.y;
+    o.z += __uint_as_float(r[4 * i + 2]) + b.z;
+    o.w += __uint_as_float(r[4 * i + 3]) + b.w;
+    dst[i] = o;
+  }
+}
+
+template <int BN, int EPI, int DH, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const GemmParams p) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
@@ -68,6 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const int cluster_id = blockIdx.x / CG;
+  const int num_clusters = gridDim.x / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -76,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], kEpiWarps * CG);  // every epilogue warp of the pair arrives on the leader
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -86,11 +166,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, S::kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, S::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, S::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) {
+    cluster_sync();  // barrier inits and the TMEM allocation are visible to the peer
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -98,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_kb = (p.K + kBK - 1) / kBK;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (each CTA loads its own A rows and B half) ----------------
     if (elect_one_sync()) {
       const uint64_t pol_a = l2_policy_evict_normal();
       const uint64_t pol_b = l2_policy_evict_last();  // weights are re-read by every m-block
@@ -106,9 +195,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int fills = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
         const int m_blk = tile / p.num_n_blocks;
         const int n_blk = tile - m_blk * p.num_n_blocks;
+        const int a_row = m_blk * (128 * CG) + 128 * static_cast<int>(rank);
+        const int b_row = n_blk * BN + S::kBRows * static_cast<int>(rank);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer)) {
             ok = false;
@@ -116,9 +207,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
-          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-          tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, m_blk * kBM, pol_a);
-          tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, n_blk * BN, pol_b);
+          if constexpr (CG == 2) {
+            if (rank == 0) mbar_arrive_expect_tx_cluster(&full[stage], 2 * S::kStageBytes);
+            const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBK, a_row, pol_a);
+            tma_load_2d_pair(sb, &tmap_b, leader_full, kb * kBK, b_row, pol_b);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+            tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, a_row, pol_a);
+            // B arrives as two half tiles (the tensor map's box is BN/2 rows).
+            tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, b_row, pol_b);
+            tma_load_2d(sb + S::kBBytes / 2, &tmap_b, &full[stage], kb * kBK, b_row + BN / 2, pol_b);
+          }
           ++fills;
           if (++stage == S::kStages) {
             stage = 0;
@@ -126,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!ok) {
+      if (!ok && (CG == 1 || rank == 0)) {
         // Let the copies this thread may still have in flight (its last kStages fills) land
         // before the CTA exits; each wait is bounded as well.
         int s = stage;
@@ -141,14 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (elect_one_sync()) {
-      constexpr uint32_t idesc = umma_idesc_f16(kBM, BN);
+    // ---------------- MMA issuer (the leader CTA of a pair) ----------------
+    if ((CG == 1 || rank == 0) && elect_one_sync()) {
+      constexpr uint32_t idesc = umma_idesc_f16(128 * CG, BN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, p.err, kDevTimeoutMma)) {
@@ -167,36 +267,62 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + S::kABytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            umma_f16(d_tmem, umma_sdesc_sw128(a_addr + k * 32), umma_sdesc_sw128(b_addr + k * 32), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+            const uint64_t ad = umma_sdesc_sw128(a_addr + k * 32);
+            const uint64_t bd = umma_sdesc_sw128(b_addr + k * 32);
+            if constexpr (CG == 2) {
+              umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            } else {
+              umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
-          umma_commit(&empty[stage]);
+          if constexpr (CG == 2) {
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          } else {
+            umma_commit(&empty[stage]);
+          }
           if (++stage == S::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        umma_commit(&acc_full[buf]);
+        if constexpr (CG == 2) {
+          umma_commit_pair(mapa_shared(smem_u32(&acc_full[buf]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&acc_full[buf]), 1));
+        } else {
+          umma_commit(&acc_full[buf]);
+        }
       }
       if (!ok) {
         // Wait (bounded) for every MMA this thread issued before tensor memory is released.
-        umma_commit(drain);
+        if constexpr (CG == 2) {
+          umma_commit_pair(mapa_shared(smem_u32(drain), 0));
+        } else {
+          umma_commit(drain);
+        }
         mbar_wait(drain, 0, p.err, kDevTimeoutMma);
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32) belong to this warp
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int quarter = warp & 3;             // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int half = (warp - 2) >> 2;         // which half of the tile's columns
+    constexpr int kChunk = (EPI == kEpiQkvRope) ? DH : 16;
+    constexpr int kSplit = ((BN / 2) / kChunk) * kChunk;
+    const int c_begin = half ? kSplit : 0;
+    const int c_end = half ? BN : kSplit;
     const int row_in_tile = quarter * 32 + lane;
+    const uint32_t leader_acc_empty0 =
+        (CG == 2) ? mapa_shared(smem_u32(&acc_empty[0]), 0) : smem_u32(&acc_empty[0]);
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], acc_phase, p.err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int m = m_blk * kBM + row_in_tile;
+      const int m = m_blk * (128 * CG) + 128 * static_cast<int>(rank) + row_in_tile;
       const bool row_ok = m < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(buf * S::kAccStride);
@@ -206,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int HALF = DH / 2;
         const int pos = row_ok ? __ldg(p.pos + m) : 0;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += DH) {
+        for (int c = c_begin; c < c_end; c += DH) {
           uint32_t r[DH];
 #pragma unroll
           for (int i = 0; i < DH / 8; ++i) tmem_ld8(t_row + c + 8 * i, r + 8 * i);
@@ -231,77 +357,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < DH / 8; ++i) store_f16x8(dst + 8 * i, v + 8 * i);
           }
         }
-      } else {
+      } else if constexpr (EPI == kEpiResidF32) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = c_begin; c < c_end; c += 16) {
+          float4 x[4];
+          if (row_ok) resid16_load(p, m, n0 + c, x);
           uint32_t r[16];
           tmem_ld16(t_row + c, r);
           tmem_ld_wait();
+          if (row_ok) resid16_store(p, m, n0 + c, r, x);
+        }
+      } else {
+        int c = c_begin;
+#pragma unroll 1
+        for (; c + 32 <= c_end; c += 32) {
+          uint32_t r[16], r2[16];
+          tmem_ld16(t_row + c, r);
+          tmem_ld16(t_row + c + 16, r2);
+          tmem_ld_wait();
           if (row_ok) {
-            const int n = n0 + c;
-            float v[16];
-            if (p.bias) {
-              const float4* b4 = reinterpret_cast<const float4*>(p.bias + n);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float4 b = __ldg(b4 + i);
-                v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + b.x;
-                v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + b.y;
-                v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + b.z;
-                v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + b.w;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-            }
-            if constexpr (EPI == kEpiGeluF16) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = gelu_as(v[i]);
-              __half* dst = static_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + n;
-              store_f16x8(dst, v);
-              store_f16x8(dst + 8, v + 8);
-            } else {
-              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
-              if constexpr (EPI == kEpiResidF32) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  float4 x = dst[i];
-                  x.x += v[4 * i + 0];
-                  x.y += v[4 * i + 1];
-                  x.z += v[4 * i + 2];
-                  x.w += v[4 * i + 3];
-                  dst[i] = x;
-                }
-              } else {
-                if constexpr (EPI == kEpiGeluF32) {
-#pragma unroll
-                  for (int i = 0; i < 16; ++i) v[i] = gelu_as(v[i]);
-                }
-#pragma unroll
-                for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-              }
-            }
+            epi16<EPI>(p, m, n0 + c, r);
+            epi16<EPI>(p, m, n0 + c + 16, r2);
           }
+        }
+        if (c < c_end) {
+          uint32_t r[16];
+          tmem_ld16(t_row + c, r);
+          tmem_ld_wait();
+          if (row_ok) epi16<EPI>(p, m, n0 + c, r);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) {
+        if constexpr (CG == 2) {
+          mbar_arrive_cluster(leader_acc_empty0 + static_cast<uint32_t>(buf * sizeof(uint64_t)));
+        } else {
+          mbar_arrive(&acc_empty[buf]);
+        }
+      }
     }
   }
 
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the peer no longer reads this CTA's smem or barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, S::kTmemCols);
+    if constexpr (CG == 2) {
+      tmem_dealloc_pair(tmem_base, S::kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, S::kTmemCols);
+    }
   }
 }
 
-template <int BN, int EPI, int DH>
+template <int BN, int EPI, int DH, int CG>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms,
                        cudaStream_t stream) {
-  using S = GemmShape<BN>;
-  auto kern = gemm_tc_kernel<BN, EPI, DH>;
+  using S = GemmShape<BN, CG>;
+  auto kern = gemm_tc_kernel<BN, EPI, DH, CG>;
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
@@ -311,36 +425,54 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
     if (dev < 64) configured |= (1ull << dev);
   }
   const int tiles = p.num_m_blocks * p.num_n_blocks;
-  const int grid = tiles < num_sms ? tiles : num_sms;
-  if (grid <= 0) return cudaSuccess;
-  kern<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, tb, p);
-  return cudaGetLastError();
+  const int clusters = tiles < num_sms / CG ? tiles : num_sms / CG;
+  if (clusters <= 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(clusters * CG, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = S::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
 }
 
-template <int BN>
+template <int BN, int CG>
 cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, int epi, int dh, const GemmParams& p,
                          int num_sms, cudaStream_t s) {
   switch (epi) {
-    case kEpiGeluF16: return launch_one<BN, kEpiGeluF16, 0>(ta, tb, p, num_sms, s);
-    case kEpiResidF32: return launch_one<BN, kEpiResidF32, 0>(ta, tb, p, num_sms, s);
-    case kEpiGeluF32: return launch_one<BN, kEpiGeluF32, 0>(ta, tb, p, num_sms, s);
-    case kEpiStoreF32: return launch_one<BN, kEpiStoreF32, 0>(ta, tb, p, num_sms, s);
+    case kEpiGeluF16: return launch_one<BN, kEpiGeluF16, 0, CG>(ta, tb, p, num_sms, s);
+    case kEpiResidF32: return launch_one<BN, kEpiResidF32, 0, CG>(ta, tb, p, num_sms, s);
+    case kEpiGeluF32: return launch_one<BN, kEpiGeluF32, 0, CG>(ta, tb, p, num_sms, s);
+    case kEpiStoreF32: return launch_one<BN, kEpiStoreF32, 0, CG>(ta, tb, p, num_sms, s);
     case kEpiQkvRope:
       if constexpr (BN % 64 == 0) {
-        if (dh == 64) return launch_one<BN, kEpiQkvRope, 64>(ta, tb, p, num_sms, s);
+        if (dh == 64) return launch_one<BN, kEpiQkvRope, 64, CG>(ta, tb, p, num_sms, s);
       }
       if constexpr (BN % 32 == 0) {
-        if (dh == 32) return launch_one<BN, kEpiQkvRope, 32>(ta, tb, p, num_sms, s);
+        if (dh == 32) return launch_one<BN, kEpiQkvRope, 32, CG>(ta, tb, p, num_sms, s);
       }
       if constexpr (BN % 24 == 0) {
-        if (dh == 24) return launch_one<BN, kEpiQkvRope, 24>(ta, tb, p, num_sms, s);
+        if (dh == 24) return launch_one<BN, kEpiQkvRope, 24, CG>(ta, tb, p, num_sms, s);
       }
       if constexpr (BN % 16 == 0) {
-        if (dh == 16) return launch_one<BN, kEpiQkvRope, 16>(ta, tb, p, num_sms, s);
+        if (dh == 16) return launch_one<BN, kEpiQkvRope, 16, CG>(ta, tb, p, num_sms, s);
       }
       return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
+}
+
+template <int BN>
+cudaError_t dispatch_cg(const CUtensorMap& ta, const CUtensorMap& tb, int epi, int dh, int cg, const GemmParams& p,
+                        int num_sms, cudaStream_t s) {
+  return cg == 2 ? dispatch_epi<BN, 2>(ta, tb, epi, dh, p, num_sms, s)
+                 : dispatch_epi<BN, 1>(ta, tb, epi, dh, p, num_sms, s);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -395,23 +527,30 @@ int gemm_pick_bn_any(int N) {
 }
 
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int head_dim, GemmParams p,
-                        int num_sms, cudaStream_t stream) {
+                        int num_sms, cudaStream_t stream, int cta_pair) {
   if (p.M <= 0) return cudaSuccess;
   if (bn <= 0 || p.N % bn || p.K <= 0) return cudaErrorInvalidValue;
-  p.num_m_blocks = (p.M + kBM - 1) / kBM;
+  // The CTA pair needs the wide tiles and at least two 128-row blocks of work.
+  const int cg = (cta_pair && bn >= 128 && p.M > 128) ? 2 : 1;
+  p.num_m_blocks = (p.M + 128 * cg - 1) / (128 * cg);
   p.num_n_blocks = p.N / bn;
   switch (bn) {
-    case 256: return dispatch_epi<256>(ta, tb, epi, head_dim, p, num_sms, stream);
-    case 240: return dispatch_epi<240>(ta, tb, epi, head_dim, p, num_sms, stream);
-    case 192: return dispatch_epi<192>(ta, tb, epi, head_dim, p, num_sms, stream);
-    case 160: return dispatch_epi<160>(ta, tb, epi, head_dim, p, num_sms, stream);
-    case 128: return dispatch_epi<128>(ta, tb, epi, head_dim, p, num_sms, stream);
+    case 256: return dispatch_cg<256>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
+    case 240: return dispatch_cg<240>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
+    case 192: return dispatch_cg<192>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
+    case 160: return dispatch_cg<160>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
+    case 128: return dispatch_cg<128>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
     // Narrow tiles serve the plain fp32-output GEMM only (odd output widths of esm_matmul_tiled).
-    case 96: return epi == kEpiStoreF32 ? launch_one<96, kEpiStoreF32, 0>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
-    case 64: return epi == kEpiStoreF32 ? launch_one<64, kEpiStoreF32, 0>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
-    case 48: return epi == kEpiStoreF32 ? launch_one<48, kEpiStoreF32, 0>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
-    case 32: return epi == kEpiStoreF32 ? launch_one<32, kEpiStoreF32, 0>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
-    case 16: return epi == kEpiStoreF32 ? launch_one<16, kEpiStoreF32, 0>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+    case 96:
+      return epi == kEpiStoreF32 ? launch_one<96, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+    case 64:
+      return epi == kEpiStoreF32 ? launch_one<64, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+    case 48:
+      return epi == kEpiStoreF32 ? launch_one<48, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+    case 32:
+      return epi == kEpiStoreF32 ? launch_one<32, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+    case 16:
+      return epi == kEpiStoreF32 ? launch_one<16, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }

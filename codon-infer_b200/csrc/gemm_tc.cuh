@@ -38,8 +38,9 @@ int gemm_pick_bn(int N, int head_dim);
 int gemm_pick_bn_any(int N);
 
 // C[M, N] = A[M, K] . B[N, K]^T with the requested epilogue; A and B are fp16 K-major behind the
-// tensor maps (A box 128 rows, B box `bn` rows). Persistent grid of min(tiles, num_sms) CTAs.
+// tensor maps (A box 128 rows, B box bn/2 rows). Persistent grid of at most num_sms CTAs; with
+// cta_pair != 0 (and bn >= 128, M > 128) tiles of 256 rows run on CTA pairs (tcgen05 cta_group::2).
 cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int head_dim,
-                        GemmParams p, int num_sms, cudaStream_t stream);
+                        GemmParams p, int num_sms, cudaStream_t stream, int cta_pair);
 
 }  // namespace esm

@@ -314,6 +314,36 @@ __global__ void scatter_rows_kernel(const float* __restrict__ src, const int32_t
   }
 }
 
+// CANONICAL_AAS token ids: A C D E F G H I K L M N P Q R S T V W Y.
+__constant__ int kCanonicalIds[20] = {5, 23, 13, 9, 18, 6, 21, 12, 15, 4, 20, 17, 14, 16, 10, 8, 11, 7, 22, 19};
+
+__global__ void dms_score_kernel(const float* __restrict__ logits, int V, const int32_t* __restrict__ tok_row,
+                                 const int32_t* __restrict__ wt_tok, int n, float* __restrict__ deltas,
+                                 float* __restrict__ entropy) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= n) return;
+  const float* lg = logits + static_cast<size_t>(tok_row[v]) * V;
+  float mx = -INFINITY;
+  for (int i = 4; i <= 23; ++i) mx = fmaxf(mx, lg[i]);
+  float se = 0.0f;
+  for (int i = 4; i <= 23; ++i) se += expf(lg[i] - mx);
+  const float lse = mx + logf(se);
+  float h = 0.0f;
+  for (int i = 4; i <= 23; ++i) {
+    const float lp = lg[i] - lse;
+    const float pa = expf(lp);
+    if (pa > 1e-12f) h -= pa * lp;
+  }
+  entropy[v] = h;
+  const int wt = wt_tok[v];
+  // log_softmax_canonical leaves -inf outside 4..=23, so a non-canonical wild type gives -inf - x.
+  const float lwt = (wt >= 4 && wt <= 23) ? lg[wt] - lse : -INFINITY;
+  for (int c = 0; c < 20; ++c) {
+    const int aa = kCanonicalIds[c];
+    deltas[static_cast<size_t>(v) * 20 + c] = (aa == wt) ? 0.0f : (lg[aa] - lse) - lwt;
+  }
+}
+
 int row_blocks(int T) { return (T + kRowWarps - 1) / kRowWarps; }
 
 }  // namespace
@@ -404,6 +434,13 @@ cudaError_t launch_lm_decoder(const float* in, int T, int d, int do_ln, const fl
   if (T <= 0) return cudaSuccess;
   if (d % 4 || d > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
   lm_decoder_kernel<<<row_blocks(T), 32 * kRowWarps, 0, s>>>(in, T, d, do_ln, ln_w, ln_b, W, bias, V, logits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dms_score(const float* logits, int V, const int32_t* tok_row, const int32_t* wt_tok, int n,
+                             float* deltas, float* entropy, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  dms_score_kernel<<<(n + 127) / 128, 128, 0, s>>>(logits, V, tok_row, wt_tok, n, deltas, entropy);
   return cudaGetLastError();
 }
 

@@ -1,6 +1,7 @@
 // Launchers of the memory-bound kernels around the GEMMs and of the attention kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -60,6 +61,13 @@ cudaError_t launch_lm_decoder(const float* in, int T, int d, int do_ln, const fl
 cudaError_t launch_scatter_rows(const float* src, const int32_t* cu_seqlens, int B, int Lmax, int C, float* dst,
                                 cudaStream_t s);
 
+// Masked-marginal scores of n variants (run_pipeline_dms_with_mode, src/pipeline.rs:111-174):
+// for variant v, logits row tok_row[v] of the packed [*, V] logits -> log_softmax_canonical over
+// ids 4..=23 (src/lib.rs:4426-4441), Shannon entropy, and deltas[v, c] = logP(aa_c) - logP(wt) in
+// CANONICAL_AAS order (src/benchmark.rs:702-707), 0 for the wild type.
+cudaError_t launch_dms_score(const float* logits, int V, const int32_t* tok_row, const int32_t* wt_tok, int n,
+                             float* deltas, float* entropy, cudaStream_t s);
+
 // ---- attention ------------------------------------------------------------------------------
 struct AttnParams {
   const __half* qkv;       // [T, 3d]: q | k | v, head h at columns h*dh of each part
@@ -70,8 +78,13 @@ struct AttnParams {
   int n_work;
   int T, d, H, dh;
   float scale;             // 1/sqrt(dh)
+  int* err;                // device error word (bounded waits of the tcgen05 kernel)
 };
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s);
+// tcgen05 attention for head_dim 64: work items are (sequence, 128-row query tile); tm_q / tm_kv
+// are fp16 tensor maps over qkv [T, 3d] with 64-column boxes of 128 / 64 rows.
+cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
+                                cudaStream_t s);
 
 // Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
 // recomputes P = softmax(q k^T * scale) tile by tile from the saved LSE, adds w * P into the

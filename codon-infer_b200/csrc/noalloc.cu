@@ -115,7 +115,7 @@ extern "C" int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const v
   // end with zeros, so no padded copies are needed.
   CUtensorMap ta, tb;
   if (!esm::make_tmap_f16(&ta, x16, static_cast<uint64_t>(seq_len), in_dim, in_dim, 128) ||
-      !esm::make_tmap_f16(&tb, w16, static_cast<uint64_t>(out_dim), in_dim, in_dim, static_cast<uint32_t>(bn)))
+      !esm::make_tmap_f16(&tb, w16, static_cast<uint64_t>(out_dim), in_dim, in_dim, static_cast<uint32_t>(bn / 2)))
     return ESM_ECUDA;
   esm::GemmParams p{};
   p.M = seq_len;
@@ -125,7 +125,7 @@ extern "C" int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const v
   p.out = out;
   p.ldo = n_pad;
   p.err = slot->err;
-  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, slot->num_sms, s);
+  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, slot->num_sms, s, 1);
   if (e == cudaSuccess && padded_out)
     e = cudaMemcpy2DAsync(d_out, static_cast<size_t>(out_dim) * 4, out, static_cast<size_t>(n_pad) * 4,
                           static_cast<size_t>(out_dim) * 4, seq_len, cudaMemcpyDeviceToDevice, s);

@@ -30,6 +30,9 @@ TENSOR_NAMES = (
 )
 MATRICES = ("wq", "wk", "wv", "wo", "fc1_w", "fc2_w")
 PROFILE_KINDS = ("dequant", "norm", "gemm", "attention", "contact", "head")
+# CANONICAL_AAS order of the mutational-scan columns (src/benchmark.rs:702-707).
+CANONICAL_AAS = "ACDEFGHIKLMNPQRSTVWY"
+CANONICAL_IDS = (5, 23, 13, 9, 18, 6, 21, 12, 15, 4, 20, 17, 14, 16, 10, 8, 11, 7, 22, 19)
 
 
 class EsmError(RuntimeError):
@@ -106,6 +109,7 @@ def lib() -> ctypes.CDLL:
             "esm_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
             "esm_forward_device": [vp, vp, vp, i32, vp, vp, vp, vp, vp, i32],
             "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
+            "esm_dms_masked_marginal": [vp, vp, i32, i32, vp, vp],
             "esm_check_device": [vp],
             "esm_profile_enable": [vp, i32],
             "esm_profile_read": [vp, i32, vp, vp, vp, vp],
@@ -346,6 +350,16 @@ class Model:
         self._chk(lib().esm_forward_device(self._ctx, ptr(d_tokens), _p(cu), cu.size - 1, ptr(d_logits),
                                            ptr(d_hidden), ptr(d_contacts), ptr(d_layer_hidden), s, int(sync)),
                   "esm_forward_device")
+
+    def dms_masked_marginal(self, residues, window_size: int = 0):
+        """Masked-marginal deep mutational scan of one sequence (residue token ids, no <cls>/<eos>).
+        Returns (deltas [n, 20] in CANONICAL_AAS order, entropy [n])."""
+        r = np.ascontiguousarray(residues, dtype=np.int32)
+        deltas = np.empty((r.size, 20), dtype=np.float32)
+        ent = np.empty(r.size, dtype=np.float32)
+        self._chk(lib().esm_dms_masked_marginal(self._ctx, _p(r), r.size, window_size, _p(deltas), _p(ent)),
+                  "esm_dms_masked_marginal")
+        return deltas, ent
 
     def matmul_tiled(self, dtype: int, x, w, bias, in_dim: int, out_dim: int) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32)

@@ -131,6 +131,17 @@ int esm_forward_device(esm_ctx* ctx, const int32_t* d_tokens, const int32_t* h_c
                        float* d_logits, float* d_hidden, float* d_contacts, float* d_layer_hidden,
                        void* stream, int32_t sync);
 
+/* In-silico deep mutational scan, masked-marginal mode (run_pipeline_dms_with_mode with
+ * DmsScoringMode::MaskedMarginal, src/pipeline.rs:76-175): for every position p of the residue
+ * tokens (ids 4..30, no <cls>/<eos>) the window around p (same centring rule and window_size
+ * semantics as the reference; 0 = whole sequence) is encoded, position p is replaced by <mask>,
+ * and the logits at p give log_softmax_canonical, the Shannon entropy entropy[p] and
+ * deltas[p, c] = logP(aa_c) - logP(wt) for the 20 CANONICAL_AAS (A C D E F G H I K L M N P Q R S T
+ * V W Y; 0 for the wild type). All n masked variants run as batches of independent sequences
+ * through the forward, limited by the reserved workspace. Outputs are HOST buffers. */
+int esm_dms_masked_marginal(esm_ctx* ctx, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
+                            float* entropy);
+
 /* matmul_tiled_{fp32,q8,q4}_parallel (src/lib.rs:4803-4827, 4870-4894, 4937-4961) on the GPU, from
  * HOST buffers: out[p, i] = sum_k W[i, k] * x[p, k] + bias[i] for p < seq_len, i < out_dim.
  * w is FP32 [out_dim, in_dim] or rows of BlockQ8_0 / BlockQ4_0 (dtype); x is FP32 [seq_len, in_dim];
