@@ -3,15 +3,15 @@
 // sequences, keys past a sequence's end masked, O in fp16, optional per-row log-sum-exp), which
 // replaces the reference attention loop (src/lib.rs:5206-5301).
 //
-// One CTA per (sequence, 128-query tile, head); 192 threads; two CTAs per SM.
+// One CTA per (sequence, 128-query tile, head); 192 threads; three CTAs per SM.
 //   warp 0      TMA producer: Q tile once, then 64-key K and V tiles into a 2-stage ring.
 //   warp 1      tcgen05.mma issuer (one thread): S = Q K^T (M 128, N 64, K 64) into tensor memory,
 //               then O_j = P_j V_j (M 128, N 64, K 64) with V as an MN-major operand.
 //   warps 2..5  softmax, one query row per thread: read S from tensor memory, online max/sum in
-//               fp32, P = exp2(S*scale*log2e - m) rounded to fp16 into shared memory in the
-//               128-byte-swizzled K-major layout the MMA reads, and O accumulated in registers
-//               as O = O*alpha + O_j.
-// Tensor memory: S in columns [0, 64), O_j in [64, 128). All waits are bounded.
+//               fp32 (exp2 on the special-function unit), P rounded to fp16 into shared memory in
+//               the 128-byte-swizzled K-major layout the MMA reads. O accumulates across tiles in
+//               tensor memory; it is rescaled there only when a row max grows past the threshold.
+// Tensor memory: S in columns [0, 64), O in [64, 128). All waits are bounded.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -31,8 +31,12 @@ constexpr int kOffV = kOffK + 2 * kKVBytes;
 constexpr int kOffP = kOffV + 2 * kKVBytes;
 constexpr int kOffBar = kOffP + kPBytes;
 constexpr int kSmemAt = kOffBar + 256 + 1024;
-constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kTmemCols = 128;  // S [0, 64), O [64, 128)
 constexpr float kLog2e = 1.4426950408889634f;
+// The running max used for P is refreshed only when a row's max grows by more than 2^8 (in the
+// exp2 domain); until then P <= 256, exact in fp16's relative precision, and O and l share the
+// stale max, so O / l and the log-sum-exp are unchanged.
+constexpr float kRescaleThreshold = 8.0f;
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -43,6 +47,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x on the special-function unit (the PTX ex2.approx instruction; relative error ~2^-22).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -61,7 +83,15 @@ __device__ __forceinline__ uint64_t umma_sdesc_sw128_mn(uint32_t saddr) {
   return d;
 }
 
-__global__ void __launch_bounds__(kThreadsAt, 2)
+// Pipeline per 64-key tile j (all waits bounded):
+//   MMA:     S = Q K_j^T        after K_j landed and the softmax read S_{j-1}        -> s_full
+//            O += P V_j         after P_j was written (O accumulates in tensor memory) -> o_full
+//   softmax: read S_j (-> s_free); when a row max jumped past the threshold, wait for the previous
+//            O += P V and rescale O in tensor memory; P_j = exp2(S c - m) into shared memory once
+//            the previous P V has consumed the buffer (-> p_full).
+// o_full can run at most one completion ahead of the softmax's waits (P V_{j+1} needs p_full of
+// tile j+1), so parity waits stay unambiguous even where a wait is skipped.
+__global__ void __launch_bounds__(kThreadsAt, 3)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
                         const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -74,9 +104,8 @@ __global__ void __launch_bounds__(kThreadsAt, 2)
   uint64_t* s_free = bars + 6;
   uint64_t* p_full = bars + 7;
   uint64_t* o_full = bars + 8;
-  uint64_t* o_free = bars + 9;
-  uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int2 wk = p.work[blockIdx.x];
@@ -95,7 +124,6 @@ __global__ void __launch_bounds__(kThreadsAt, 2)
     mbar_init(s_free, 4);
     mbar_init(p_full, 4);
     mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -107,8 +135,8 @@ __global__ void __launch_bounds__(kThreadsAt, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem;        // S: columns [0, 64)
-  const uint32_t t_o = tmem + 64;   // O_j: columns [64, 128)
+  const uint32_t t_s = tmem;       // S: columns [0, 64)
+  const uint32_t t_o = tmem + 64;  // O: columns [64, 128)
 
   if (warp == 0) {
     if (elect_one_sync()) {
@@ -155,12 +183,12 @@ __global__ void __launch_bounds__(kThreadsAt, 2)
           umma_f16(t_s, umma_sdesc_sw128(q_addr + k * 32), umma_sdesc_sw128(k_addr + k * 32), idesc_qk, k > 0);
         umma_commit(s_full);
         if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(o_free, (j - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + kOffV + st * kKVBytes);
 #pragma unroll
         for (int k = 0; k < kKV / 16; ++k)
-          umma_f16(t_o, umma_sdesc_sw128(p_addr + k * 32), umma_sdesc_sw128_mn(v_addr + k * 2048), idesc_pv, k > 0);
+          umma_f16(t_o, umma_sdesc_sw128(p_addr + k * 32), umma_sdesc_sw128_mn(v_addr + k * 2048), idesc_pv,
+                   (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(&kv_empty[st]);
       }
@@ -175,16 +203,45 @@ __global__ void __launch_bounds__(kThreadsAt, 2)
     const int r = quarter * 32 + lane;  // row inside the tile = TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float c = p.scale * kLog2e;
-    float o[kD];
-#pragma unroll
-    for (int i = 0; i < kD; ++i) o[i] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+    float mc = -INFINITY;  // running max in the exp2 domain (max score * c)
+    float l = 0.0f;
     uint8_t* prow = smem + kOffP + r * 128;
     const int sw = r & 7;
     bool ok = true;
     for (int j = 0; j < nkv && ok; ++j) {
-      // 1. fold O_{j-1} = P_{j-1} V_{j-1} (scale m_{j-1}) into the register accumulator.
-      if (j > 0) {
+      if (!mbar_wait(s_full, j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      const int kvalid = len - j * kKV;  // keys of this tile inside the sequence (> 0)
+      // Pass 1: row max (32 columns at a time keeps registers low). c > 0, so the max of the
+      // scaled scores is c times the max of the raw ones; only the last tile needs the key mask.
+      float mraw = -INFINITY;
+      if (kvalid >= kKV) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t t[32];
+          tmem_ld32(t_s + lane_off + half * 32, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(t[i]));
+        }
+      } else {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t t[32];
+          tmem_ld32(t_s + lane_off + half * 32, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (half * 32 + i < kvalid) mraw = fmaxf(mraw, __uint_as_float(t[i]));
+        }
+      }
+      const float mx = mraw * c;
+      if (j == 0) {
+        mc = mx;
+      } else if (__any_sync(0xffffffffu, mx - mc > kRescaleThreshold)) {
+        // Refresh the max of this warp's rows: O (after the previous P V) and l scale by alpha.
+        const float m_new = fmaxf(mc, mx);
+        const float alpha = fast_exp2(mc - m_new);
         if (!mbar_wait(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -193,87 +250,76 @@ __global__ void __launch_bounds__(kThreadsAt, 2)
           tmem_ld32(t_o + lane_off + half * 32, t);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[half * 32 + i] += __uint_as_float(t[i]);
+          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+          tmem_st32(t_o + lane_off + half * 32, t);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_free);
+        tmem_st_wait();
+        l *= alpha;
+        mc = m_new;
       }
-      // 2. scores of tile j.
-      if (!mbar_wait(s_full, j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
-      tc_fence_after();
-      float s[kKV];
-      {
-        uint32_t t[32];
-        tmem_ld32(t_s + lane_off, t);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(t[i]);
-        tmem_ld32(t_s + lane_off + 32, t);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(t[i]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);  // the next Q K^T may overwrite S
-      const int kbase = j * kKV;
-      if (kbase + kKV > len) {
-#pragma unroll
-        for (int i = 0; i < kKV; ++i)
-          if (kbase + i >= len) s[i] = -INFINITY;
-      }
-      float mx = s[0];
-#pragma unroll
-      for (int i = 1; i < kKV; ++i) mx = fmaxf(mx, s[i]);
-      const float m_new = fmaxf(m, mx);
-      const float ms = m_new * c;
-      const float alpha = exp2f(m * c - ms);  // 0 on the first tile (m = -inf)
+      // The previous P V must have consumed the P buffer before it is overwritten.
+      if (j > 0 && !mbar_wait(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      // Pass 2: P = exp2(S c - m) in fp16 into the 128-byte swizzled K-major tile (16-byte chunk k
+      // of row r at chunk k ^ (r & 7)); keys past the sequence end get P = 0.
       float rs = 0.0f;
+      const bool full_tile = kvalid >= kKV;
 #pragma unroll
-      for (int i = 0; i < kKV; ++i) {
-        s[i] = exp2f(s[i] * c - ms);
-        rs += s[i];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t t[32];
+        tmem_ld32(t_s + lane_off + half * 32, t);
+        tmem_ld_wait();
+        if (!full_tile) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (half * 32 + i >= kvalid) t[i] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float e[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            e[u] = fast_exp2(fmaf(__uint_as_float(t[8 * k + u]), c, -mc));
+            rs += e[u];
+          }
+          __half2 hv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) hv[u] = __floats2half2_rn(e[2 * u], e[2 * u + 1]);
+          const int chunk = half * 4 + k;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ sw) << 4)) = *reinterpret_cast<uint4*>(hv);
+        }
       }
-      l = l * alpha + rs;
-      m = m_new;
-#pragma unroll
-      for (int i = 0; i < kD; ++i) o[i] *= alpha;
-      // 3. P_j (fp16) into the swizzled K-major tile: 16-byte chunk k of row r lands at chunk k ^ (r & 7).
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        __half2 hv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(s[8 * k + 2 * e], s[8 * k + 2 * e + 1]);
-        *reinterpret_cast<uint4*>(prow + ((k ^ sw) << 4)) = *reinterpret_cast<uint4*>(hv);
-      }
+      l += rs;
+      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) {
+        mbar_arrive(s_free);  // the next Q K^T may overwrite S
+        mbar_arrive(p_full);
+      }
     }
     if (ok && mbar_wait(o_full, (nkv - 1) & 1, p.err, kDevTimeoutEpilogue)) {
       tc_fence_after();
+      const int row = q0 + r;
+      const float inv = 1.0f / l;
+      __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * kD;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t t[32];
         tmem_ld32(t_o + lane_off + half * 32, t);
         tmem_ld_wait();
+        if (row < len) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[half * 32 + i] += __uint_as_float(t[i]);
-      }
-      const int row = q0 + r;
-      if (row < len) {
-        const float inv = 1.0f / l;
-        __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * kD;
+          for (int k = 0; k < 4; ++k) {
+            __half2 hv[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          __half2 hv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(o[8 * k + 2 * e] * inv, o[8 * k + 2 * e + 1] * inv);
-          *reinterpret_cast<uint4*>(dst + 8 * k) = *reinterpret_cast<uint4*>(hv);
+            for (int e = 0; e < 4; ++e)
+              hv[e] = __floats2half2_rn(__uint_as_float(t[8 * k + 2 * e]) * inv,
+                                        __uint_as_float(t[8 * k + 2 * e + 1]) * inv);
+            *reinterpret_cast<uint4*>(dst + half * 32 + 8 * k) = *reinterpret_cast<uint4*>(hv);
+          }
         }
-        if (p.lse) p.lse[static_cast<size_t>(h) * p.T + start + row] = m * p.scale + logf(l);
       }
+      if (row < len && p.lse) p.lse[static_cast<size_t>(h) * p.T + start + row] = (mc + log2f(l)) / kLog2e;
     }
   }
   __syncthreads();

@@ -15,6 +15,7 @@ enum DeviceError : int {
   kDevTimeoutMma = 2,
   kDevTimeoutEpilogue = 4,
   kDevBadArgs = 8,
+  kDevTimeoutProbe = 16,
 };
 
 // Every spin-wait on an mbarrier gives up after this many nanoseconds of %globaltimer.
@@ -72,13 +73,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for phase `parity` of `bar`. Returns false (and records `code` in *err) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Bounded wait for phase `parity` of `bar`. Returns false (and records `code` in *err) once
+// `limit_ns` of %globaltimer have passed without the phase completing.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicOr(err, code);
       return false;
     }

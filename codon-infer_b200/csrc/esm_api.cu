@@ -1192,6 +1192,15 @@ int esm_profile_read(esm_ctx* c, int32_t kind, double* total_ms, int64_t* launch
   return ESM_OK;
 }
 
+int esm_probe_wait_timeout(esm_ctx* c, int32_t limit_ms) {
+  if (!c || limit_ms <= 0 || limit_ms > 2000) return fail(c, ESM_EINVAL, "limit_ms must be in (0, 2000]");
+  std::lock_guard<std::mutex> lk(c->mu);
+  ESM_CUDA(cudaSetDevice(c->device));
+  ESM_CUDA(esm::launch_wait_probe(c->d_err, static_cast<uint64_t>(limit_ms) * 1000000ull, c->stream));
+  ESM_CUDA(cudaStreamSynchronize(c->stream));
+  return check_device_word(c);
+}
+
 int esm_check_device(esm_ctx* c) {
   if (!c) return ESM_EINVAL;
   std::lock_guard<std::mutex> lk(c->mu);

@@ -88,9 +88,11 @@ __device__ __forceinline__ void epi16(const GemmParams& p, int m, int n, const u
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
   }
-  if constexpr (EPI == kEpiGeluF16) {
+  if constexpr (EPI == kEpiGeluF16 || EPI == kEpiStoreF16) {
+    if constexpr (EPI == kEpiGeluF16) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = gelu_fast(v[i]);
+      for (int i = 0; i < 16; ++i) v[i] = gelu_fast(v[i]);
+    }
     __half* dst = static_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + n;
     store_f16x8(dst, v);
     store_f16x8(dst + 8, v + 8);
@@ -328,7 +330,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                              static_cast<uint32_t>(buf * S::kAccStride);
       const int n0 = n_blk * BN;
 
-      if constexpr (EPI == kEpiQkvRope) {
+      if constexpr (EPI == kEpiQkvRope && (DH / 2) % 16 == 0) {
+        // head_dim 32 / 64: rotate 16 (j, j + DH/2) pairs per step; the bias and cos/sin rows are
+        // requested (float4) before the tensor-memory wait so their latency overlaps it.
+        constexpr int HALF = DH / 2;
+        const int pos = row_ok ? __ldg(p.pos + m) : 0;
+        __half* dst_row = static_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo;
+        // The (cos, sin) row of this thread's position is the same for every head: load it once.
+        float4 cs_all[HALF / 2];
+        if (row_ok && n0 + c_begin < p.rope_cols) {
+          const float4* cs_row = reinterpret_cast<const float4*>(p.rope + static_cast<size_t>(pos) * HALF);
+#pragma unroll
+          for (int i = 0; i < HALF / 2; ++i) cs_all[i] = __ldg(cs_row + i);
+        }
+#pragma unroll 1
+        for (int c = c_begin; c < c_end; c += DH) {
+          const int n = n0 + c;
+          if (n < p.rope_cols) {
+#pragma unroll
+            for (int sub = 0; sub < HALF; sub += 16) {
+              float4 b0[4], b1[4];
+              if (row_ok) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  b0[i] = __ldg(reinterpret_cast<const float4*>(p.bias + n + sub) + i);
+                  b1[i] = __ldg(reinterpret_cast<const float4*>(p.bias + n + HALF + sub) + i);
+                }
+              }
+              const float4* cs = cs_all + sub / 2;
+              uint32_t r0[16], r1[16];
+              tmem_ld16(t_row + c + sub, r0);
+              tmem_ld16(t_row + c + HALF + sub, r1);
+              tmem_ld_wait();
+              if (row_ok) {
+                const float* bb0 = reinterpret_cast<const float*>(b0);
+                const float* bb1 = reinterpret_cast<const float*>(b1);
+                const float* cc = reinterpret_cast<const float*>(cs);  // (cos, sin) pairs
+                float y0[16], y1[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float x0 = __uint_as_float(r0[j]) + bb0[j];
+                  const float x1 = __uint_as_float(r1[j]) + bb1[j];
+                  y0[j] = x0 * cc[2 * j] - x1 * cc[2 * j + 1];
+                  y1[j] = x1 * cc[2 * j] + x0 * cc[2 * j + 1];
+                }
+                store_f16x8(dst_row + n + sub, y0);
+                store_f16x8(dst_row + n + sub + 8, y0 + 8);
+                store_f16x8(dst_row + n + HALF + sub, y1);
+                store_f16x8(dst_row + n + HALF + sub + 8, y1 + 8);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int sub = 0; sub < DH; sub += 16) {
+              uint32_t r[16];
+              tmem_ld16(t_row + c + sub, r);
+              tmem_ld_wait();
+              if (row_ok) epi16<kEpiStoreF16>(p, m, n + sub, r);
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiQkvRope) {
         constexpr int HALF = DH / 2;
         const int pos = row_ok ? __ldg(p.pos + m) : 0;
 #pragma unroll 1

@@ -13,6 +13,7 @@ enum GemmEpilogue : int {
   kEpiResidF32 = 2, // out f32 += acc + bias            (residual stream update)
   kEpiGeluF32 = 3,  // out f32 = gelu(acc + bias)
   kEpiStoreF32 = 4, // out f32 = acc + bias
+  kEpiStoreF16 = 5, // out f16 = acc + bias (the V columns of the QKV epilogue)
 };
 
 struct GemmParams {

@@ -344,6 +344,14 @@ __global__ void dms_score_kernel(const float* __restrict__ logits, int V, const 
   }
 }
 
+__global__ void wait_probe_kernel(int* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  // Phase 0 never completes: nobody arrives on the barrier.
+  mbar_wait(&bar, 0, err, kDevTimeoutProbe, limit_ns);
+}
+
 int row_blocks(int T) { return (T + kRowWarps - 1) / kRowWarps; }
 
 }  // namespace
@@ -441,6 +449,11 @@ cudaError_t launch_dms_score(const float* logits, int V, const int32_t* tok_row,
                              float* deltas, float* entropy, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   dms_score_kernel<<<(n + 127) / 128, 128, 0, s>>>(logits, V, tok_row, wt_tok, n, deltas, entropy);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait_probe(int* err, uint64_t limit_ns, cudaStream_t s) {
+  wait_probe_kernel<<<1, 1, 0, s>>>(err, limit_ns);
   return cudaGetLastError();
 }
 

@@ -68,6 +68,10 @@ cudaError_t launch_scatter_rows(const float* src, const int32_t* cu_seqlens, int
 cudaError_t launch_dms_score(const float* logits, int V, const int32_t* tok_row, const int32_t* wt_tok, int n,
                              float* deltas, float* entropy, cudaStream_t s);
 
+// One thread waits, with the kernels' bounded mbarrier wait and a limit of `limit_ns`, on a phase
+// that nothing completes; on timeout it records kDevTimeoutProbe in *err and returns.
+cudaError_t launch_wait_probe(int* err, uint64_t limit_ns, cudaStream_t s);
+
 // ---- attention ------------------------------------------------------------------------------
 struct AttnParams {
   const __half* qkv;       // [T, 3d]: q | k | v, head h at columns h*dh of each part

@@ -111,6 +111,7 @@ def lib() -> ctypes.CDLL:
             "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
             "esm_dms_masked_marginal": [vp, vp, i32, i32, vp, vp],
             "esm_check_device": [vp],
+            "esm_probe_wait_timeout": [vp, i32],
             "esm_profile_enable": [vp, i32],
             "esm_profile_read": [vp, i32, vp, vp, vp, vp],
         }
@@ -383,6 +384,10 @@ class Model:
                                              ctypes.byref(by)), "esm_profile_read")
             out[name] = {"ms": ms.value, "launches": n.value, "flops": fl.value, "bytes": by.value}
         return out
+
+    def probe_wait_timeout(self, limit_ms: int = 50) -> int:
+        """Runs the bounded-wait self-test; returns the status (ESM_ETIMEOUT when it works)."""
+        return lib().esm_probe_wait_timeout(self._ctx, limit_ms)
 
     def check_device(self) -> None:
         self._chk(lib().esm_check_device(self._ctx), "esm_check_device")

@@ -186,6 +186,12 @@ int esm_profile_enable(esm_ctx* ctx, int32_t enable);
 /* Totals for one class since the last enable (synchronizes with the recorded events). */
 int esm_profile_read(esm_ctx* ctx, int32_t kind, double* total_ms, int64_t* launches, double* flops, double* bytes);
 
+/* Self-test of the device failure path (no counterpart in the reference): one thread waits, with
+ * the same bounded mbarrier wait the kernels use but a limit of limit_ms milliseconds, on a phase
+ * that nothing completes. Returns ESM_ETIMEOUT when the wait gave up as designed, after which the
+ * context is usable again. No trap, fault or unbounded loop is involved. */
+int esm_probe_wait_timeout(esm_ctx* ctx, int32_t limit_ms);
+
 /* Device error word check: ESM_ETIMEOUT if a kernel's bounded wait gave up since the last call. */
 int esm_check_device(esm_ctx* ctx);
 

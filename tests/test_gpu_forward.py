@@ -176,3 +176,15 @@ def test_capacity_and_argument_errors(esm):
     out = m.forward(esm.random_sequences(2, 50))
     assert np.isfinite(out["logits"]).all()
     m.check_device()
+
+
+def test_device_wait_timeout_reports_and_recovers(esm):
+    # A bounded device wait that nothing satisfies gives up after 50 ms, sets the context's error
+    # word, and the host sees ESM_ETIMEOUT; the context then runs a forward normally.
+    cfg = esm.EsmConfig(320, 1280, 1, 20, arch=0)
+    m, _, _ = build(esm, cfg, esm.DTYPE_Q4_0, contact=False)
+    m.reserve(64, 1, 64)
+    assert m.probe_wait_timeout(50) == esm.ESM_ETIMEOUT
+    m.check_device()  # the error word was cleared
+    out = m.forward(esm.random_sequences(1, 64))
+    assert np.isfinite(out["logits"]).all()
