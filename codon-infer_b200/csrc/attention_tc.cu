@@ -216,14 +216,19 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
       // scaled scores is c times the max of the raw ones; only the last tile needs the key mask.
       float mraw = -INFINITY;
       if (kvalid >= kKV) {
+        // Tree reduction: 8 independent partial maxima keep the dependency chains short.
+        float pm[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t t[32];
           tmem_ld32(t_s + lane_off + half * 32, t);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(t[i]));
+          for (int i = 0; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(t[i]));
         }
+        mraw = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       } else {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -261,7 +266,9 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
       if (j > 0 && !mbar_wait(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
       // Pass 2: P = exp2(S c - m) in fp16 into the 128-byte swizzled K-major tile (16-byte chunk k
       // of row r at chunk k ^ (r & 7)); keys past the sequence end get P = 0.
-      float rs = 0.0f;
+      float rsp[8];  // independent partial row sums
+#pragma unroll
+      for (int u = 0; u < 8; ++u) rsp[u] = 0.0f;
       const bool full_tile = kvalid >= kKV;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -279,7 +286,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             e[u] = fast_exp2(fmaf(__uint_as_float(t[8 * k + u]), c, -mc));
-            rs += e[u];
+            rsp[u] += e[u];
           }
           __half2 hv[4];
 #pragma unroll
@@ -288,7 +295,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
           *reinterpret_cast<uint4*>(prow + ((chunk ^ sw) << 4)) = *reinterpret_cast<uint4*>(hv);
         }
       }
-      l += rs;
+      l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();

@@ -486,11 +486,7 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
     if (e != cudaSuccess) return e;
     if (dev < 64) configured |= (1ull << dev);
   }
-  const int tiles = p.num_m_blocks * p.num_n_blocks;
-  const int clusters = tiles < num_sms / CG ? tiles : num_sms / CG;
-  if (clusters <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(clusters * CG, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = S::kSmemBytes;
   cfg.stream = stream;
@@ -501,6 +497,24 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // Tiles are split statically over the persistent CTAs, so every cluster must be resident at
+  // once: a cluster of two needs two free SMs in one GPC, and the count of clusters that fit at the
+  // same time can be below num_sms / 2.
+  static int resident[64] = {0};
+  int max_clusters = num_sms / CG;
+  if (CG > 1 && dev < 64) {
+    if (resident[dev] == 0) {
+      cfg.gridDim = dim3(max_clusters * CG, 1, 1);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = max_clusters;
+      resident[dev] = n;
+    }
+    max_clusters = resident[dev] < max_clusters ? resident[dev] : max_clusters;
+  }
+  const int tiles = p.num_m_blocks * p.num_n_blocks;
+  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  if (clusters <= 0) return cudaSuccess;
+  cfg.gridDim = dim3(clusters * CG, 1, 1);
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
 }
 

@@ -3,6 +3,8 @@
 //
 // All are HBM-bound: one warp per token row, vectorised 16-byte accesses, grids sized to the
 // number of rows (every row is independent).
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -42,6 +44,22 @@ __device__ __forceinline__ void row_stats(const float4 (&v)[MAXC], int nchunks, 
 
 constexpr int kMaxChunks = 20;  // d <= 2560 = 32 lanes * 4 floats * 20
 
+// Row kernels are instantiated for the float4 chunks a lane holds, ceil(d / 128) for d = 320 .. 2560,
+// so the register footprint (and with it the occupancy) follows the model width.
+template <typename F>
+void row_dispatch(int d, F&& launch) {
+  switch ((d / 4 + 31) / 32) {
+    case 1: launch(std::integral_constant<int, 1>{}); break;
+    case 2: launch(std::integral_constant<int, 2>{}); break;
+    case 3: launch(std::integral_constant<int, 3>{}); break;
+    case 4: launch(std::integral_constant<int, 4>{}); break;
+    case 5: launch(std::integral_constant<int, 5>{}); break;
+    case 8: launch(std::integral_constant<int, 8>{}); break;
+    case 10: launch(std::integral_constant<int, 10>{}); break;
+    default: launch(std::integral_constant<int, kMaxChunks>{}); break;
+  }
+}
+
 __global__ void seq_setup_kernel(const int32_t* __restrict__ tokens, const int32_t* __restrict__ cu, int32_t* pos,
                                  int32_t* seq_of, float* embed_scale) {
   const int b = blockIdx.x;
@@ -66,6 +84,7 @@ __global__ void seq_setup_kernel(const int32_t* __restrict__ tokens, const int32
   }
 }
 
+template <int NCH>
 __global__ void embed_ln_kernel(const int32_t* __restrict__ tokens, const int32_t* __restrict__ seq_of,
                                 const float* __restrict__ embed_scale, const float* __restrict__ emb_f32,
                                 const uint8_t* __restrict__ emb_q8, int T, int d,
@@ -77,9 +96,9 @@ __global__ void embed_ln_kernel(const int32_t* __restrict__ tokens, const int32_
   const int tok = tokens[row];
   const float sc = embed_scale[seq_of[row]];
   const int nchunks = (d / 4 - lane + 31) / 32;
-  float4 v[kMaxChunks];
+  float4 v[NCH];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NCH; ++c) {
     if (c >= nchunks) break;
     const int e = 4 * (lane + 32 * c);
     float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -103,9 +122,9 @@ __global__ void embed_ln_kernel(const int32_t* __restrict__ tokens, const int32_
     *reinterpret_cast<float4*>(x + static_cast<size_t>(row) * d + e) = val;
   }
   float mean, inv;
-  row_stats<kMaxChunks>(v, nchunks, d, mean, inv);
+  row_stats<NCH>(v, nchunks, d, mean, inv);
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NCH; ++c) {
     if (c >= nchunks) break;
     const int e = 4 * (lane + 32 * c);
     const float4 w = *reinterpret_cast<const float4*>(ln_w + e);
@@ -119,6 +138,7 @@ __global__ void embed_ln_kernel(const int32_t* __restrict__ tokens, const int32_
   }
 }
 
+template <int NCH>
 __global__ void layernorm_kernel(const float* __restrict__ x, int T, int d, const float* __restrict__ w,
                                  const float* __restrict__ b, __half* __restrict__ out16, int ld16,
                                  float* __restrict__ out32) {
@@ -126,16 +146,16 @@ __global__ void layernorm_kernel(const float* __restrict__ x, int T, int d, cons
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const int nchunks = (d / 4 - lane + 31) / 32;
-  float4 v[kMaxChunks];
+  float4 v[NCH];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NCH; ++c) {
     if (c >= nchunks) break;
     v[c] = *reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * d + 4 * (lane + 32 * c));
   }
   float mean, inv;
-  row_stats<kMaxChunks>(v, nchunks, d, mean, inv);
+  row_stats<NCH>(v, nchunks, d, mean, inv);
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NCH; ++c) {
     if (c >= nchunks) break;
     const int e = 4 * (lane + 32 * c);
     const float4 ww = *reinterpret_cast<const float4*>(w + e);
@@ -258,6 +278,7 @@ __global__ void scatter_maps_kernel(const float* __restrict__ src, const int64_t
 }
 
 // LM head tail (src/lib.rs:5405-5428): optional LayerNorm of the row, then V dot products in fp32.
+template <int NCH>
 __global__ void lm_decoder_kernel(const float* __restrict__ in, int T, int d, int do_ln, const float* __restrict__ ln_w,
                                   const float* __restrict__ ln_b, const float* __restrict__ W,
                                   const float* __restrict__ bias, int V, float* __restrict__ logits) {
@@ -265,17 +286,17 @@ __global__ void lm_decoder_kernel(const float* __restrict__ in, int T, int d, in
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
   const int nchunks = (d / 4 - lane + 31) / 32;
-  float4 v[kMaxChunks];
+  float4 v[NCH];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NCH; ++c) {
     if (c >= nchunks) break;
     v[c] = *reinterpret_cast<const float4*>(in + static_cast<size_t>(row) * d + 4 * (lane + 32 * c));
   }
   if (do_ln) {
     float mean, inv;
-    row_stats<kMaxChunks>(v, nchunks, d, mean, inv);
+    row_stats<NCH>(v, nchunks, d, mean, inv);
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < NCH; ++c) {
       if (c >= nchunks) break;
       const int e = 4 * (lane + 32 * c);
       const float4 ww = *reinterpret_cast<const float4*>(ln_w + e);
@@ -290,7 +311,7 @@ __global__ void lm_decoder_kernel(const float* __restrict__ in, int T, int d, in
     const float* wr = W + static_cast<size_t>(o) * d;
     float s = 0.0f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < NCH; ++c) {
       if (c >= nchunks) break;
       const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + 4 * (lane + 32 * c)));
       s += (v[c].x * w4.x + v[c].y * w4.y) + (v[c].z * w4.z + v[c].w * w4.w);
@@ -368,9 +389,10 @@ cudaError_t launch_embed_ln(const int32_t* tokens, const int32_t* seq_of, const 
                             const float* ln_b, float* x, __half* xn, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (d % 32 || d > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
-  embed_ln_kernel<<<row_blocks(T), 32 * kRowWarps, 0, s>>>(tokens, seq_of, embed_scale, emb_f32,
-                                                          static_cast<const uint8_t*>(emb_q8), T, d, ln_w, ln_b, x,
-                                                          xn);
+  row_dispatch(d, [&](auto nch) {
+    embed_ln_kernel<decltype(nch)::value><<<row_blocks(T), 32 * kRowWarps, 0, s>>>(
+        tokens, seq_of, embed_scale, emb_f32, static_cast<const uint8_t*>(emb_q8), T, d, ln_w, ln_b, x, xn);
+  });
   return cudaGetLastError();
 }
 
@@ -378,7 +400,9 @@ cudaError_t launch_layernorm(const float* x, int T, int d, const float* w, const
                              float* out32, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (d % 4 || d > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
-  layernorm_kernel<<<row_blocks(T), 32 * kRowWarps, 0, s>>>(x, T, d, w, b, out16, ld16, out32);
+  row_dispatch(d, [&](auto nch) {
+    layernorm_kernel<decltype(nch)::value><<<row_blocks(T), 32 * kRowWarps, 0, s>>>(x, T, d, w, b, out16, ld16, out32);
+  });
   return cudaGetLastError();
 }
 
@@ -441,7 +465,10 @@ cudaError_t launch_lm_decoder(const float* in, int T, int d, int do_ln, const fl
                               const float* W, const float* bias, int V, float* logits, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (d % 4 || d > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
-  lm_decoder_kernel<<<row_blocks(T), 32 * kRowWarps, 0, s>>>(in, T, d, do_ln, ln_w, ln_b, W, bias, V, logits);
+  row_dispatch(d, [&](auto nch) {
+    lm_decoder_kernel<decltype(nch)::value><<<row_blocks(T), 32 * kRowWarps, 0, s>>>(in, T, d, do_ln, ln_w, ln_b, W,
+                                                                                      bias, V, logits);
+  });
   return cudaGetLastError();
 }
 
