@@ -31,12 +31,43 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "codon-infer_b200"))
 
-METRIC = "residues/sec, ESM-2 650M Q4_0 forward (64 x L=1024 per GPU)"
 UNIT = "residues/s"
+# The benchmark configurations (tokens include <cls>/<eos>). c4 is the headline and the default.
 CONFIGS = {
-    # name: (arch, dtype, batch per GPU, seq_len)
-    "c4": (3, 2, 64, 1024),
+    "c1": dict(arch=0, dtype=0, batch=1, lengths="fixed", seq_len=128, contacts=True, dms=False,
+               desc="ESM-2 8M FP32 forward, 1 x L=128, contact head on"),
+    "c2": dict(arch=1, dtype=1, batch=32, lengths="uniform", seq_len=512, min_len=64, contacts=False, dms=False,
+               desc="ESM-2 35M Q8_0 forward, 32 sequences with L in U[64, 512], right-padded"),
+    "c3": dict(arch=2, dtype=0, batch=300, lengths="fixed", seq_len=302, contacts=False, dms=True,
+               desc="ESM-2 150M FP32 masked-marginal scan: 300 single-<mask> variants of a 300-residue wild type"),
+    "c4": dict(arch=3, dtype=2, batch=64, lengths="fixed", seq_len=1024, contacts=False, dms=False,
+               desc="ESM-2 650M Q4_0 forward, 64 x L=1024 per GPU, logits out"),
+    "c5": dict(arch=4, dtype=1, batch=8, lengths="fixed", seq_len=4096, contacts=True, dms=False,
+               desc="ESM-2 3B Q8_0 forward, 8 x L=4096 per GPU, contact maps on"),
 }
+
+
+def metric_name(cfg_name, c, batch):
+    return {
+        "c4": "residues/sec, ESM-2 650M Q4_0 forward (64 x L=1024 per GPU)",
+    }.get(cfg_name, f"residues/sec, {c['desc']}")
+
+
+def workload_sequences(esm, c, batch, rank):
+    """Token sequences of one rank's batch (seeded per rank)."""
+    if c["dms"]:
+        wt = esm.random_sequences(1, c["seq_len"], seed=2000)[0]
+        out = []
+        for p in range(batch):
+            v = wt.copy()
+            v[1 + (p % (c["seq_len"] - 2))] = esm.MASK_ID
+            out.append(v)
+        return out
+    if c["lengths"] == "uniform":
+        rng = np.random.default_rng(3000 + rank)
+        lens = rng.integers(c["min_len"], c["seq_len"] + 1, size=batch)
+        return esm.random_sequences(batch, lens, seed=1000 + rank)
+    return esm.random_sequences(batch, c["seq_len"], seed=1000 + rank)
 
 
 def measured_peaks():
@@ -129,26 +160,28 @@ def run_reference(args):
     """CPU arm: the restated reference forward on the host cores, one sequence per step."""
     import esm_b200 as esm
     rank = int(os.environ.get("RANK", "0"))
-    arch, dtype, batch, seq_len = CONFIGS[args.config]
+    c = CONFIGS[args.config]
+    batch = args.batch or c["batch"]
     if rank != 0:
         return
-    cfg = esm.EsmConfig.preset(arch)
-    t = esm.quantize_tensors(esm.synth_fp32_tensors(cfg, seed=0), dtype)
+    cfg = esm.EsmConfig.preset(c["arch"])
+    t = esm.quantize_tensors(esm.synth_fp32_tensors(cfg, seed=0), c["dtype"])
     threads = os.cpu_count() or 1
+    seq_len = c["seq_len"]
     for w in range(args.warmup):
-        cpu_forward_rate(cfg, dtype, t, seq_len, 1000 + w, threads)
+        cpu_forward_rate(cfg, c["dtype"], t, seq_len, 1000 + w, threads)
     t0 = time.perf_counter()
     for k in range(args.steps):
-        cpu_forward_rate(cfg, dtype, t, seq_len, 2000 + k, threads)
+        cpu_forward_rate(cfg, c["dtype"], t, seq_len, 2000 + k, threads)
     dt = time.perf_counter() - t0
     value = args.steps * seq_len / dt
-    sample = f"1 sequence x L={seq_len} per step (of the {batch} x {seq_len} per-GPU batch), all layers"
+    sample = f"1 sequence x L={seq_len} per step (of the {batch}-sequence per-GPU batch), all layers"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "impl": "reference", "metric": metric_name(args.config, c, batch), "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded uniform residues, random-init N(0,0.02) weights)",
-        "config": {"workload": f"ESM-2 650M Q4_0 forward, {seq_len}-token sequences", "seq_len": seq_len},
+        "config": {"workload": c["desc"] + f" (CPU: {seq_len}-token sequences)", "seq_len": seq_len},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -171,22 +204,31 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
-    arch, dtype, batch, seq_len = CONFIGS[args.config]
-    if args.batch:
-        batch = args.batch  # smaller per-GPU batch for profiler captures only
+    c = CONFIGS[args.config]
+    arch, dtype, seq_len = c["arch"], c["dtype"], c["seq_len"]
+    batch = args.batch or c["batch"]  # a smaller per-GPU batch is for profiler captures only
     cfg = esm.EsmConfig.preset(arch)
     t32 = esm.synth_fp32_tensors(cfg, seed=0)
     tensors = esm.quantize_tensors(t32, dtype)
     del t32
     model = esm.Model(local)
     model.load_tensors(cfg, dtype, tensors)
-    T = batch * seq_len
-    model.reserve(T, batch, seq_len)
-    seqs = esm.random_sequences(batch, seq_len, seed=1000 + rank)
-    host_tokens = np.stack(seqs).astype(np.int32)
-    cu = np.arange(batch + 1, dtype=np.int32) * seq_len
-    d_tokens = torch.from_numpy(host_tokens.reshape(-1)).to(dev)
+    if c["contacts"]:
+        cw = (np.random.default_rng(7).standard_normal(cfg.n_layers * cfg.n_heads) * 0.1).astype(np.float32)
+        model.set_contact_head(cw, 0.0)
+    seqs = workload_sequences(esm, c, batch, rank)
+    lengths = np.array([len(q) for q in seqs], dtype=np.int32)
+    T = int(lengths.sum())
+    Lmax = int(lengths.max())
+    model.reserve(T, batch, Lmax, contacts=c["contacts"])
+    host_tokens = np.zeros((batch, Lmax), dtype=np.int32)
+    for i, q in enumerate(seqs):
+        host_tokens[i, : len(q)] = q
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    d_tokens = torch.from_numpy(np.concatenate(seqs).astype(np.int32)).to(dev)
     d_logits = torch.empty(T, cfg.vocab_size, device=dev)
+    n_map = int(sum(max(int(L) - 2, 0) ** 2 for L in lengths))
+    d_contacts = torch.empty(max(n_map, 1), device=dev) if c["contacts"] else None
     gathered = torch.empty(world * T, cfg.vocab_size, device=dev) if world > 1 else None
     # A dedicated stream: the forward is enqueued on it and the CUDA events are recorded on it.
     # (torch's default stream has handle 0, which the C ABI reads as "the context's own stream".)
@@ -194,7 +236,7 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
 
     def step():
-        model.forward_device(d_tokens, cu, d_logits, stream=stream)
+        model.forward_device(d_tokens, cu, d_logits, d_contacts=d_contacts, stream=stream)
         if world > 1:
             dist.all_gather_into_tensor(gathered, d_logits)
 
@@ -228,14 +270,14 @@ def run_ours(args):
     if ms <= 0.0:
         raise SystemExit("timed region is empty: the forward did not run on the timed stream")
 
-    # End to end through the host API: pinned host tokens in, logits back to host every step.
+    # End to end through the host API: pinned host tokens in, results back to host every step.
     host_tok = torch.from_numpy(host_tokens).pin_memory()
-    host_lengths = np.full(batch, seq_len, dtype=np.int32)
-    host_logits = torch.empty(batch, seq_len, cfg.vocab_size, dtype=torch.float32).pin_memory()
+    host_logits = torch.empty(batch, Lmax, cfg.vocab_size, dtype=torch.float32).pin_memory()
     tok_np, log_np = host_tok.numpy(), host_logits.numpy()
+    d2h = batch * Lmax * cfg.vocab_size * 4 + (batch * max(Lmax - 2, 0) ** 2 * 4 if c["contacts"] else 0)
 
     def e2e_step():
-        model.forward(tok_np, lengths=host_lengths, logits_out=log_np)
+        model.forward(tok_np, lengths=lengths, logits_out=log_np, want_contacts=c["contacts"])
 
     e2e_steps = max(1, min(args.steps, 5))
     e2e_step()
@@ -250,10 +292,19 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e_value = world * T * e2e_steps / e2e_s
+    dms_rate = None
+    if c["dms"]:
+        # The public mutational-scan call on the same wild type: masked variants built, run and
+        # scored inside the library, scores [n, 20] back to host.
+        residues = esm.random_sequences(1, c["seq_len"], seed=2000)[0][1:-1]  # the wild type
+        model.dms_masked_marginal(residues)
+        t0 = time.perf_counter()
+        model.dms_masked_marginal(residues)
+        dms_rate = len(residues) / (time.perf_counter() - t0)
 
     # Per-kernel-class device time of one step (CUDA events around each launch, its own stream).
     model.profile_enable(True)
-    model.forward_device(d_tokens, cu, d_logits, stream=stream)
+    model.forward_device(d_tokens, cu, d_logits, d_contacts=d_contacts, stream=stream)
     torch.cuda.synchronize(dev)
     prof = model.profile_read()
     model.profile_enable(False)
@@ -286,20 +337,21 @@ def run_ours(args):
         threads = os.cpu_count() or 1
         rate = cpu_forward_rate(cfg, dtype, tensors, seq_len, 4242, threads)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"1 sequence x L={seq_len}, full 33-layer forward (CPU restatement of the reference)"}
+               "sample": f"1 sequence x L={seq_len}, full {cfg.n_layers}-layer forward "
+                         "(CPU restatement of the reference)"}
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16 operands / f32 accumulate (Q4_0 weights)",
+            "metric": metric_name(args.config, c, batch), "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 operands / f32 accumulate (" + ["FP32", "Q8_0", "Q4_0"][dtype] + " weights)",
             "data": "synthetic (seeded uniform residues, random-init N(0,0.02) weights)",
-            "config": {"workload": f"ESM-2 650M Q4_0 forward, {batch} x L={seq_len} per GPU, logits out",
-                       "batch_per_gpu": batch, "seq_len": seq_len,
+            "config": {"workload": c["desc"], "batch_per_gpu": batch, "seq_len": Lmax, "tokens_per_gpu": T,
                        "parallelism": f"sequence-sharded x{world}, logits all-gather",
-                       "l2": "no flush: the per-step working set (activations ~2.5 GB) exceeds the 126 MB L2"},
+                       "l2": "no flush: the per-step working set (activations, weights) exceeds the 126 MB L2"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(host_tokens.nbytes + 4 * batch),
-                    "d2h_bytes_per_step": int(batch * seq_len * cfg.vocab_size * 4), "steps": e2e_steps},
+                    "d2h_bytes_per_step": int(d2h), "steps": e2e_steps},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roofline,
             "achieved_model_tflops": total_flops / (ms / args.steps / 1000.0) / 1e12,
@@ -307,6 +359,8 @@ def run_ours(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if dms_rate is not None:
+            line["dms_variants_per_s"] = dms_rate
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:
@@ -319,7 +373,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c4")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c4",
+                    help="c4 (headline, default): 650M Q4_0 64 x 1024; c1/c2/c3/c5: the other benchmark configs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling captures)")
     args = ap.parse_args()
