@@ -1,0 +1,285 @@
+// C++ host API over the B200 C ABI that keeps codon-infer's own interface for the encoder forward:
+// the names, argument meaning and failure behaviour of EsmConfig, EsmWeights{,Q8,Q4}, Block{Q8,Q4}_0,
+// BidirectionalRunState, Tokenizer, log_softmax_canonical and the forward_bidirectional* family
+// (codon-infer v1.12.0, src/lib.rs). A Rust caller binds the C ABI directly (see the integration
+// notes); C++ callers and the C++ tests use this header.
+//
+// Failure behaviour mirrors the reference: loader errors are thrown as IoError carrying the
+// io::ErrorKind the reference would return (NotFound, InvalidData, UnexpectedEof); misuse that
+// panics in the reference (a sequence longer than the state's max_len) throws std::logic_error.
+// Weights live on one GPU: every EsmWeights* object owns one device context.
+#pragma once
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <fstream>
+#include <limits>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/esm_b200.h"
+
+namespace codon_infer {
+
+enum class ErrorKind { NotFound, InvalidData, UnexpectedEof, Other };
+
+class IoError : public std::runtime_error {
+ public:
+  IoError(ErrorKind k, const std::string& m) : std::runtime_error(m), kind_(k) {}
+  ErrorKind kind() const { return kind_; }
+
+ private:
+  ErrorKind kind_;
+};
+
+enum class EsmModelArch { Esm2_8M = 0, Esm2_35M = 1, Esm2_150M = 2, Esm2_650M = 3, Esm2_3B = 4 };
+
+// EsmConfig, src/lib.rs:76-150.
+struct EsmConfig {
+  size_t dim = 0, hidden_dim = 0, n_layers = 0, n_heads = 0, vocab_size = 33, max_seq_len = 1024;
+  EsmModelArch arch = EsmModelArch::Esm2_8M;
+
+  static EsmConfig preset(EsmModelArch a) {
+    esm_config c;
+    if (esm_config_preset(static_cast<int32_t>(a), &c) != ESM_OK) throw std::invalid_argument("unknown arch");
+    return from_c(c);
+  }
+  static EsmConfig esm2_8m() { return preset(EsmModelArch::Esm2_8M); }
+  static EsmConfig esm2_35m() { return preset(EsmModelArch::Esm2_35M); }
+  static EsmConfig esm2_150m() { return preset(EsmModelArch::Esm2_150M); }
+  static EsmConfig esm2_650m() { return preset(EsmModelArch::Esm2_650M); }
+  static EsmConfig esm2_3b() { return preset(EsmModelArch::Esm2_3B); }
+  size_t head_dim() const { return dim / n_heads; }
+
+  // EsmConfig::detect_from_file, src/lib.rs:277-297.
+  static EsmConfig detect_from_file(const std::string& path) {
+    esm_config c;
+    int32_t dt = 0;
+    const int rc = esm_config_detect_file(path.c_str(), &c, &dt);
+    if (rc == ESM_EIO) throw IoError(ErrorKind::NotFound, "cannot open " + path);
+    if (rc != ESM_OK) throw IoError(ErrorKind::InvalidData, "unrecognized ESM-2 weights file " + path);
+    return from_c(c);
+  }
+
+  esm_config to_c() const {
+    esm_config c;
+    c.dim = static_cast<int32_t>(dim);
+    c.hidden_dim = static_cast<int32_t>(hidden_dim);
+    c.n_layers = static_cast<int32_t>(n_layers);
+    c.n_heads = static_cast<int32_t>(n_heads);
+    c.vocab_size = static_cast<int32_t>(vocab_size);
+    c.max_seq_len = static_cast<int32_t>(max_seq_len);
+    c.arch = static_cast<int32_t>(arch);
+    return c;
+  }
+  static EsmConfig from_c(const esm_config& c) {
+    EsmConfig e;
+    e.dim = c.dim;
+    e.hidden_dim = c.hidden_dim;
+    e.n_layers = c.n_layers;
+    e.n_heads = c.n_heads;
+    e.vocab_size = c.vocab_size;
+    e.max_seq_len = c.max_seq_len;
+    e.arch = static_cast<EsmModelArch>(c.arch);
+    return e;
+  }
+};
+
+// BlockQ8_0 / BlockQ4_0, src/lib.rs:640-673, 1043-1088 (byte layout of the on-disk formats).
+struct BlockQ8_0 {
+  float d;
+  int8_t qs[32];
+  static BlockQ8_0 quantize(const float* src) {
+    BlockQ8_0 b;
+    esm_quantize_q8(src, 32, &b);
+    return b;
+  }
+  void dequantize_to(float* dst) const {
+    for (int i = 0; i < 32; ++i) dst[i] = static_cast<float>(qs[i]) * d;
+  }
+};
+struct BlockQ4_0 {
+  float d;
+  uint8_t qs[16];
+  static BlockQ4_0 quantize(const float* src) {
+    BlockQ4_0 b;
+    esm_quantize_q4(src, 32, &b);
+    return b;
+  }
+  void dequantize_to(float* dst) const {
+    for (int j = 0; j < 16; ++j) {
+      dst[j] = static_cast<float>(static_cast<int>(qs[j] & 0x0F) - 8) * d;
+      dst[j + 16] = static_cast<float>(static_cast<int>((qs[j] >> 4) & 0x0F) - 8) * d;
+    }
+  }
+};
+static_assert(sizeof(BlockQ8_0) == 36 && sizeof(BlockQ4_0) == 20, "block sizes of the CODQ format");
+
+inline std::vector<BlockQ8_0> quantize_slice_to_q8(const std::vector<float>& src) {
+  if (src.size() % 32) throw std::logic_error("Source length must be a multiple of 32");
+  std::vector<BlockQ8_0> out(src.size() / 32);
+  esm_quantize_q8(src.data(), static_cast<int64_t>(src.size()), out.data());
+  return out;
+}
+inline std::vector<BlockQ4_0> quantize_slice_to_q4(const std::vector<float>& src) {
+  if (src.size() % 32) throw std::logic_error("Source length must be a multiple of 32");
+  std::vector<BlockQ4_0> out(src.size() / 32);
+  esm_quantize_q4(src.data(), static_cast<int64_t>(src.size()), out.data());
+  return out;
+}
+
+// Tokenizer, src/lib.rs:6509-6531.
+struct Tokenizer {
+  static std::vector<size_t> encode(const std::string& text) {
+    std::vector<int32_t> ids(text.size() + 2);
+    int32_t n = 0;
+    if (esm_tokenize(text.c_str(), ids.data(), static_cast<int32_t>(ids.size()), &n) != ESM_OK)
+      throw std::logic_error("tokenizer capacity");
+    return std::vector<size_t>(ids.begin(), ids.begin() + n);
+  }
+  // Tokenizer::decode, src/lib.rs:6523-6530: '\0' where the reference returns None.
+  static char decode(size_t id) {
+    static const char kAlphabet[] = "LAGVSERTIDPKQNFYMHWCXBUZO.-";
+    if (id >= 4 && id <= 30) return kAlphabet[id - 4];
+    return id == 32 ? '*' : '\0';
+  }
+};
+
+// log_softmax_canonical, src/lib.rs:4426-4441.
+inline std::vector<float> log_softmax_canonical(const float* logits) {
+  std::vector<float> out(33, -std::numeric_limits<float>::infinity());
+  float mx = -std::numeric_limits<float>::infinity();
+  for (int i = 4; i <= 23; ++i) mx = logits[i] > mx ? logits[i] : mx;
+  float s = 0.0f;
+  for (int i = 4; i <= 23; ++i) s += std::exp(logits[i] - mx);
+  const float lse = mx + std::log(s);
+  for (int i = 4; i <= 23; ++i) out[i] = logits[i] - lse;
+  return out;
+}
+
+// A weight set resident on one GPU (the device context that owns it).
+class DeviceWeights {
+ public:
+  DeviceWeights(const DeviceWeights&) = delete;
+  DeviceWeights& operator=(const DeviceWeights&) = delete;
+  ~DeviceWeights() {
+    if (ctx_) esm_ctx_destroy(ctx_);
+  }
+  esm_ctx* ctx() const { return ctx_; }
+  int32_t dtype() const { return dtype_; }
+  const EsmConfig& config() const { return cfg_; }
+  size_t reserved_len() const { return reserved_len_; }
+  bool reserved_contacts() const { return reserved_contacts_; }
+  void reserve(size_t max_len, bool contacts) {
+    check(esm_reserve(ctx_, static_cast<int32_t>(max_len), 1, static_cast<int32_t>(max_len), contacts ? 1 : 0));
+    reserved_len_ = max_len;
+    reserved_contacts_ = contacts;
+  }
+  // The contact regression head (EsmConfig::contact_head_weights, src/lib.rs:154-177) is an input
+  // here: n_layers * n_heads weights (layer-major) and the bias.
+  void set_contact_head(const std::vector<float>& weights, float bias) {
+    check(esm_set_contact_head(ctx_, weights.data(), static_cast<int32_t>(weights.size()), bias));
+  }
+  void check(int rc) const {
+    if (rc == ESM_OK) return;
+    const std::string msg = esm_last_error(ctx_);
+    if (rc == ESM_EIO) throw IoError(ErrorKind::UnexpectedEof, msg);
+    if (rc == ESM_EFORMAT) throw IoError(ErrorKind::InvalidData, msg);
+    if (rc == ESM_ECAPACITY) throw std::logic_error(msg);
+    throw IoError(ErrorKind::Other, msg);
+  }
+
+ protected:
+  DeviceWeights(int device, const EsmConfig& cfg, int32_t dtype) : cfg_(cfg), dtype_(dtype) {
+    if (esm_ctx_create(device, &ctx_) != ESM_OK) throw IoError(ErrorKind::Other, "no usable B200 device");
+  }
+  EsmConfig cfg_;
+  int32_t dtype_;
+  esm_ctx* ctx_ = nullptr;
+  size_t reserved_len_ = 0;
+  bool reserved_contacts_ = false;
+
+  void load_file(const std::string& path) {
+    const esm_config c = cfg_.to_c();
+    check(esm_load_file(ctx_, path.c_str(), &c));
+  }
+};
+
+// EsmWeights / EsmWeightsQ8 / EsmWeightsQ4 (src/lib.rs:299-307, 676-687, 1125-1136): from_file
+// accepts exactly what the reference loaders accept (CODQ header or header-less layouts).
+#define CODON_INFER_WEIGHTS(NAME, DTYPE)                                                              \
+  class NAME : public DeviceWeights {                                                                 \
+   public:                                                                                            \
+    static std::unique_ptr<NAME> from_file(const std::string& path, const EsmConfig& cfg, int device = 0) { \
+      if (!std::ifstream(path, std::ios::binary)) throw IoError(ErrorKind::NotFound, "cannot open " + path); \
+      std::unique_ptr<NAME> w(new NAME(device, cfg));                                                 \
+      w->load_file(path);                                                                             \
+      if (w->dtype_actual() != DTYPE) throw IoError(ErrorKind::InvalidData, "unexpected weight dtype"); \
+      return w;                                                                                       \
+    }                                                                                                 \
+                                                                                                      \
+   private:                                                                                           \
+    NAME(int device, const EsmConfig& cfg) : DeviceWeights(device, cfg, DTYPE) {}                     \
+    int32_t dtype_actual() const { return dtype_; }                                                   \
+  };
+CODON_INFER_WEIGHTS(EsmWeights, ESM_DTYPE_FP32)
+CODON_INFER_WEIGHTS(EsmWeightsQ8, ESM_DTYPE_Q8_0)
+CODON_INFER_WEIGHTS(EsmWeightsQ4, ESM_DTYPE_Q4_0)
+#undef CODON_INFER_WEIGHTS
+
+// BidirectionalRunState, src/lib.rs:2488-2544: the outputs the pipelines read.
+struct BidirectionalRunState {
+  size_t max_len;
+  std::vector<float> x;              // [max_len * dim]   LN_f(x) after the forward
+  std::vector<float> logits;         // [max_len * vocab]
+  std::vector<float> contact_probs;  // [max_len * max_len], row-major over the first n*n entries
+  bool compute_contacts = true;
+
+  BidirectionalRunState(const EsmConfig& cfg, size_t max_len_)
+      : max_len(max_len_),
+        x(max_len_ * cfg.dim),
+        logits(max_len_ * cfg.vocab_size),
+        contact_probs(max_len_ * max_len_) {}
+};
+
+namespace detail {
+inline void run(const std::vector<size_t>& tokens, DeviceWeights& w, BidirectionalRunState& state) {
+  const size_t L = tokens.size();
+  if (L > state.max_len)  // src/lib.rs:5106 (assert!)
+    throw std::logic_error("Sequence length " + std::to_string(L) + " exceeds max_len " +
+                           std::to_string(state.max_len));
+  const size_t n = L >= 2 ? L - 2 : 0;
+  const bool contacts = state.compute_contacts && n > 0;
+  if (w.reserved_len() < state.max_len || (contacts && !w.reserved_contacts())) w.reserve(state.max_len, contacts);
+  std::vector<int32_t> toks(tokens.begin(), tokens.end());
+  const int32_t len = static_cast<int32_t>(L);
+  std::vector<float> cmap(contacts ? n * n : 0);
+  w.check(esm_forward(w.ctx(), toks.data(), &len, 1, len, state.logits.data(), state.x.data(),
+                      contacts ? cmap.data() : nullptr));
+  if (contacts) std::copy(cmap.begin(), cmap.end(), state.contact_probs.begin());
+}
+}  // namespace detail
+
+// forward_bidirectional{,_parallel} (FP32), _q8, _q4 (src/lib.rs:5078-5095, 5442-5448, 5790-5798).
+// num_threads is accepted for signature compatibility; the work runs on the GPU.
+inline void forward_bidirectional_parallel(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeights& w,
+                                           BidirectionalRunState& state, size_t /*num_threads*/) {
+  detail::run(tokens, w, state);
+}
+inline void forward_bidirectional(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeights& w,
+                                  BidirectionalRunState& state) {
+  detail::run(tokens, w, state);
+}
+inline void forward_bidirectional_q8(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeightsQ8& w,
+                                     BidirectionalRunState& state, size_t /*num_threads*/) {
+  detail::run(tokens, w, state);
+}
+inline void forward_bidirectional_q4(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeightsQ4& w,
+                                     BidirectionalRunState& state, size_t /*num_threads*/) {
+  detail::run(tokens, w, state);
+}
+
+}  // namespace codon_infer
