@@ -208,22 +208,33 @@ class DeviceWeights {
   }
 };
 
+// dtype field of a CODQ header (magic, version, dtype as little-endian u32 at bytes 0, 4, 8), or
+// -1 for a header-less file. Throws NotFound when the file cannot be opened.
+inline int32_t codq_dtype(const std::string& path) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) throw IoError(ErrorKind::NotFound, "cannot open " + path);
+  unsigned char h[12] = {0};
+  f.read(reinterpret_cast<char*>(h), sizeof(h));
+  if (f.gcount() < static_cast<std::streamsize>(sizeof(h)) || std::memcmp(h, "CODQ", 4) != 0) return -1;
+  return static_cast<int32_t>(h[8] | (h[9] << 8) | (h[10] << 16) | (static_cast<uint32_t>(h[11]) << 24));
+}
+
 // EsmWeights / EsmWeightsQ8 / EsmWeightsQ4 (src/lib.rs:299-307, 676-687, 1125-1136): from_file
 // accepts exactly what the reference loaders accept (CODQ header or header-less layouts).
 #define CODON_INFER_WEIGHTS(NAME, DTYPE)                                                              \
   class NAME : public DeviceWeights {                                                                 \
    public:                                                                                            \
     static std::unique_ptr<NAME> from_file(const std::string& path, const EsmConfig& cfg, int device = 0) { \
-      if (!std::ifstream(path, std::ios::binary)) throw IoError(ErrorKind::NotFound, "cannot open " + path); \
+      const int32_t file_dtype = codq_dtype(path);                                                    \
+      if (file_dtype >= 0 && file_dtype != DTYPE)                                                     \
+        throw IoError(ErrorKind::InvalidData, "CODQ dtype " + std::to_string(file_dtype) + " is not " #NAME); \
       std::unique_ptr<NAME> w(new NAME(device, cfg));                                                 \
       w->load_file(path);                                                                             \
-      if (w->dtype_actual() != DTYPE) throw IoError(ErrorKind::InvalidData, "unexpected weight dtype"); \
       return w;                                                                                       \
     }                                                                                                 \
                                                                                                       \
    private:                                                                                           \
     NAME(int device, const EsmConfig& cfg) : DeviceWeights(device, cfg, DTYPE) {}                     \
-    int32_t dtype_actual() const { return dtype_; }                                                   \
   };
 CODON_INFER_WEIGHTS(EsmWeights, ESM_DTYPE_FP32)
 CODON_INFER_WEIGHTS(EsmWeightsQ8, ESM_DTYPE_Q8_0)
