@@ -1,0 +1,278 @@
+// Contact-head accumulation on the 5th-generation tensor cores (tcgen05) for head_dim 64, the
+// ESM-2 650M and 3B shape. Same result as contact_accumulate_kernel in attention.cu; replaces the
+// per-head part of the reference contact head (accumulate_head_apc, src/lib.rs:5036-5076, called
+// for every head at 5303-5312).
+//
+// Per layer, every head h with a non-zero regression weight w_h contributes
+//   M += w_h P_h                          (P_h = softmax rows of the attention, inner block only)
+//   r_h[i] += rowsum_i(P_h) + colsum_i(P_h)   (APC sums of the symmetrised map P_h + P_h^T)
+// over the inner block (tokens 1..n, n = L - 2). P_h is recomputed from Q, K and the row
+// log-sum-exp that the attention kernel saved, so no per-head map is stored.
+//
+// The tile is computed transposed: S^T = K Q^T with M = 128 keys (tensor-memory lanes, one key per
+// thread) and N = 96 queries. A thread then owns a key column of P: its column sum accumulates in
+// a register, and it keeps 48 entries of M^T for its key in registers across all heads (96
+// queries keep the 48 accumulators, the S^T chunk and the addressing within 96 registers, the
+// limit for two 320-thread CTAs per SM). M is only ever used as M + M^T, so storing M^T in place
+// of M gives the same contacts. The row sums need no reduction: rows of P sum to one over all L
+// keys, so rowsum over the inner keys is 1 - P[i, 0] - P[i, L-1], which the threads owning keys 0
+// and L-1 add for every query.
+//
+// One CTA per (sequence, 128-key tile, 96-query tile); 320 threads; two CTAs per SM.
+//   warp 0      TMA producer: the K and Q tiles of each contributing head into a 2-stage ring.
+//   warp 1      tcgen05.mma issuer: S^T = K Q^T (M 128, N 96, K 64) into one of two TMEM buffers.
+//   warps 2..9  two warps per TMEM lane quarter, each one key per thread over 48 of the queries:
+//               exp2(S c - lse) on the special-function unit, M^T and column sums in registers; at
+//               the end M^T is staged through shared memory and added to M with coalesced rows.
+// All waits are bounded; on a timeout the error word is set and M is left untouched.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace esm {
+
+namespace {
+
+constexpr int kKeys = 128;    // keys per tile (MMA M, TMEM lanes)
+constexpr int kQry = 96;      // queries per tile (MMA N)
+constexpr int kQHalf = 48;    // queries per epilogue thread
+constexpr int kSBuf = 128;    // TMEM columns between the two S^T buffers
+constexpr int kD = 64;        // head dim (MMA K)
+constexpr int kThreadsCt = 320;
+constexpr int kKBytes = kKeys * kD * 2;  // 16 KiB
+constexpr int kQBytes = kQry * kD * 2;   // 12 KiB
+constexpr int kStageBytes = kKBytes + kQBytes;
+constexpr int kStages = 2;
+constexpr int kOffLse = kStages * kStageBytes;  // [n_heads][96] lse * log2(e) (inf outside 1..n)
+constexpr int kMaxHeads = 64;
+constexpr int kStageStride = kQry + 1;  // floats per staged M^T row (conflict-free)
+constexpr uint32_t kTmemCols = 256;     // two S^T buffers of 96 columns, 128 apart
+constexpr float kLog2e = 1.4426950408889634f;
+
+// M^T is staged over the operand ring and the log-sum-exp table once the head loop is done.
+inline int contact_tc_smem_bytes(int H) {
+  const int used = kOffLse + H * kQry * 4 + kMaxHeads * 4 + 128;
+  const int stage = kKeys * kStageStride * 4;
+  return (used > stage ? used : stage) + 1024;
+}
+
+__global__ void __launch_bounds__(kThreadsCt, 2)
+    contact_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
+                      const ContactParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* lse_s = reinterpret_cast<float*>(smem + kOffLse);
+  int* heads = reinterpret_cast<int*>(smem + kOffLse + p.H * kQry * 4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffLse + p.H * kQry * 4 + kMaxHeads * 4);
+  uint64_t* full = bars + 0;    // [2]
+  uint64_t* empty = bars + 2;   // [2]
+  uint64_t* s_full = bars + 4;  // [2]
+  uint64_t* s_free = bars + 6;  // [2]
+  uint64_t* drain = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  int* nh_s = reinterpret_cast<int*>(bars + 10);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int4 tl = p.tiles[blockIdx.x];
+  const int b = tl.x, k0 = tl.y * kKeys, q0 = tl.z * kQry;
+  const int start = p.cu_seqlens[b];
+  const int len = p.cu_seqlens[b + 1] - start;
+  const int n = len - 2;
+
+  if (threadIdx.x == 0) {
+    int nh = 0;
+    for (int h = 0; h < p.H && h < kMaxHeads; ++h)
+      if (p.w_layer[h] != 0.0f) heads[nh++] = h;
+    *nh_s = nh;
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 8);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int nh = *nh_s;
+  if (nh == 0 || n <= 0) return;
+  // Row log-sum-exps of this query tile for every contributing head, in the exp2 domain; queries
+  // outside the inner block get +inf so that their P is exactly 0.
+  for (int idx = threadIdx.x; idx < nh * kQry; idx += kThreadsCt) {
+    const int t = idx / kQry, c = idx % kQry;
+    const int i = q0 + c;
+    lse_s[idx] = (i >= 1 && i <= n) ? p.lse[static_cast<size_t>(heads[t]) * p.T + start + i] * kLog2e : INFINITY;
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  float acc[kQHalf];  // M^T[key, q0 + 48 * qh + c] summed over heads (epilogue threads)
+#pragma unroll
+  for (int c = 0; c < kQHalf; ++c) acc[c] = 0.0f;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_q);
+      const uint64_t pol = l2_policy_evict_normal();
+      int t = 0;
+      for (; t < nh; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(&empty[st], ((t >> 1) & 1) ^ 1u, p.err, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const int h = heads[t];
+        uint8_t* dst = smem + st * kStageBytes;
+        mbar_arrive_expect_tx(&full[st], kStageBytes);
+        tma_load_2d(dst, &tmap_k, &full[st], p.d + h * kD, start + k0, pol);
+        tma_load_2d(dst + kKBytes, &tmap_q, &full[st], h * kD, start + q0, pol);
+      }
+      if (!ok) {  // let the loads already in flight land before the CTA exits
+        for (int tt = (t - 2 > 0 ? t - 2 : 0); tt < t; ++tt)
+          mbar_wait(&full[tt & 1], (tt >> 1) & 1, p.err, kDevTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc = umma_idesc_f16(kKeys, kQry);
+      for (int t = 0; t < nh && ok; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(&full[st], (t >> 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (t >= 2 && !mbar_wait(&s_free[st], ((t >> 1) - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + st * kStageBytes);
+        const uint32_t q_addr = k_addr + kKBytes;
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_f16(tmem + st * kSBuf, umma_sdesc_sw128(k_addr + k * 32), umma_sdesc_sw128(q_addr + k * 32), idesc,
+                   k > 0);
+        umma_commit(&s_full[st]);
+        umma_commit(&empty[st]);
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, p.err, kDevTimeoutMma);
+      }
+    }
+  } else {
+    // ---------------- one key per thread, 48 queries per warp ----------------
+    const int quarter = warp & 3;
+    const int qh = (warp - 2) >> 2;      // which 48 queries of the tile
+    const int kr = quarter * 32 + lane;  // key row inside the tile = TMEM lane
+    const int key = k0 + kr;             // token index inside the sequence
+    const bool inner_key = key >= 1 && key <= n;
+    const bool edge_key = key == 0 || key == len - 1;  // supplies the row-sum term
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const float c = p.scale * kLog2e;
+    for (int t = 0; t < nh; ++t) {
+      const int st = t & 1;
+      if (!mbar_wait(&s_full[st], (t >> 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      const int h = heads[t];
+      const float w = p.w_layer[h];
+      const float* lrow = lse_s + t * kQry + qh * kQHalf;
+      float* rh = p.r + p.r_off[b] + static_cast<size_t>(p.head_base + h) * n;
+      float cs[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int part = 0; part < kQHalf / 16; ++part) {
+        uint32_t s[16];
+        tmem_ld16(tmem + st * kSBuf + lane_off + qh * kQHalf + part * 16, s);
+        tmem_ld_wait();
+        if (part == kQHalf / 16 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[st]);  // the MMA of head t + 2 may overwrite this buffer
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lrow + part * 16 + 4 * g);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float lu = u == 0 ? l4.x : u == 1 ? l4.y : u == 2 ? l4.z : l4.w;
+            const float pv = fast_exp2(fmaf(__uint_as_float(s[4 * g + u]), c, -lu));
+            cs[u & 1] += pv;
+            acc[part * 16 + 4 * g + u] = fmaf(w, pv, acc[part * 16 + 4 * g + u]);
+          }
+        }
+        if (edge_key) {
+          // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i.
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int i = q0 + qh * kQHalf + part * 16 + u;
+            if (i < 1 || i > n) continue;
+            const float pv = fast_exp2(fmaf(__uint_as_float(s[u]), c, -lrow[part * 16 + u]));
+            atomicAdd(rh + (i - 1), (key == 0 ? 1.0f : 0.0f) - pv);
+          }
+        }
+      }
+      if (inner_key) atomicAdd(rh + (key - 1), cs[0] + cs[1]);
+    }
+  }
+  // Every role is done with the operand ring (loads landed, MMAs complete) past this barrier.
+  const int failed = __syncthreads_or(!ok);
+  float* stage = reinterpret_cast<float*>(smem);
+  if (!failed && warp >= 2) {
+    const int kr = (warp & 3) * 32 + lane;
+    const int qh = (warp - 2) >> 2;
+#pragma unroll
+    for (int cc = 0; cc < kQHalf; ++cc) stage[kr * kStageStride + qh * kQHalf + cc] = acc[cc];
+  }
+  __syncthreads();
+  if (!failed && warp >= 2) {
+    // M^T rows of this tile: row (key - 1), columns (q0 + c - 1), inner entries only.
+    float* Mb = p.M + p.m_off[b];
+    const int wq = warp - 2;
+    for (int rr = wq; rr < kKeys; rr += 8) {
+      const int key = k0 + rr;
+      if (key < 1 || key > n) continue;
+      float* mrow = Mb + static_cast<size_t>(key - 1) * n;
+#pragma unroll
+      for (int cc = lane; cc < kQry; cc += 32) {
+        const int i = q0 + cc;
+        if (i >= 1 && i <= n) mrow[i - 1] += stage[rr * kStageStride + cc];
+      }
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+int contact_tc_tiles(int len, int4* out, int b) {
+  const int kt = (len + kKeys - 1) / kKeys, qt = (len + kQry - 1) / kQry;
+  if (out)
+    for (int i = 0; i < kt; ++i)
+      for (int j = 0; j < qt; ++j) out[i * qt + j] = make_int4(b, i, j, 0);
+  return kt * qt;
+}
+
+cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q96, const ContactParams& p,
+                              cudaStream_t s) {
+  if (p.n_tiles <= 0) return cudaSuccess;
+  if (p.dh != kD || p.H > kMaxHeads) return cudaErrorInvalidValue;
+  const int smem = contact_tc_smem_bytes(p.H);
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !(configured & (1ull << dev))) {
+    // The largest head count (64) fixes the attribute once per device.
+    cudaError_t e = cudaFuncSetAttribute(contact_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         contact_tc_smem_bytes(kMaxHeads));
+    if (e != cudaSuccess) return e;
+    if (dev < 64) configured |= (1ull << dev);
+  }
+  contact_tc_kernel<<<p.n_tiles, kThreadsCt, smem, s>>>(tm_k128, tm_q96, p);
+  return cudaGetLastError();
+}
+
+}  // namespace esm

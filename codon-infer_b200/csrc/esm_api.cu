@@ -29,7 +29,10 @@ struct esm_ctx {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   int cta_pair = 0;  // GEMM tiles on CTA pairs when ESM_GEMM_CTA_PAIR=1 (single CTAs measured faster)
-  int attn_tc = 1;   // tcgen05 attention for head_dim 64 (ESM_ATTN_TC=0 selects the mma.sync kernel)
+  // Attention kernel for head_dim 64 (ESM_ATTN_TC): 2 = tcgen05, two query tiles per CTA with P in
+  // tensor memory; 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
+  int attn_tc = 1;
+  int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
   std::string err;
   int* d_err = nullptr;
@@ -79,6 +82,7 @@ struct esm_ctx {
   float* escale = nullptr;
   int2* work = nullptr;
   int2* work128 = nullptr;
+  int2* work256 = nullptr;
   int4* ctiles = nullptr;
   int64_t* m_off = nullptr;
   int64_t* r_off = nullptr;
@@ -87,17 +91,18 @@ struct esm_ctx {
   float* a_scr = nullptr;
   float* cmap = nullptr;
   CUtensorMap tm_xn, tm_ao, tm_hb;
-  CUtensorMap tm_qkv_q, tm_qkv_kv;  // qkv [T, 3d] with 64-column boxes of 128 / 64 rows
+  CUtensorMap tm_qkv_q, tm_qkv_kv, tm_qkv_96;  // qkv [T, 3d] with 64-column boxes of 128 / 64 / 96 rows
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
   int2* h_work128 = nullptr;
+  int2* h_work256 = nullptr;
   int4* h_tiles = nullptr;
   int64_t* h_moff = nullptr;
   int64_t* h_roff = nullptr;
   cudaEvent_t plan_ev = nullptr;
   std::vector<int32_t> plan_key;
-  int plan_work = 0, plan_work128 = 0, plan_tiles = 0;
+  int plan_work = 0, plan_work128 = 0, plan_work256 = 0, plan_tiles = 0;
   // instrumentation: CUDA event pairs around each launch while profiling is on
   struct ProfRec {
     cudaEvent_t a, b;
@@ -151,11 +156,13 @@ void free_list(std::vector<void*>& list) {
 
 void free_pinned(esm_ctx* c) {
   for (void* p : {static_cast<void*>(c->h_cu), static_cast<void*>(c->h_work), static_cast<void*>(c->h_work128),
+                  static_cast<void*>(c->h_work256),
                   static_cast<void*>(c->h_tiles), static_cast<void*>(c->h_moff), static_cast<void*>(c->h_roff)})
     if (p) cudaFreeHost(p);
   c->h_cu = nullptr;
   c->h_work = nullptr;
   c->h_work128 = nullptr;
+  c->h_work256 = nullptr;
   c->h_tiles = nullptr;
   c->h_moff = nullptr;
   c->h_roff = nullptr;
@@ -349,6 +356,7 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   A(&c->escale, max_seqs);
   A(&c->work, c->work_cap);
   A(&c->work128, c->work_cap);
+  A(&c->work256, c->work_cap);
   A(&c->ctiles, c->tiles_cap);
   A(&c->m_off, max_seqs);
   A(&c->r_off, max_seqs);
@@ -372,6 +380,7 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   ESM_CUDA(cudaMallocHost(&c->h_cu, sizeof(int32_t) * (max_seqs + 1)));
   ESM_CUDA(cudaMallocHost(&c->h_work, sizeof(int2) * c->work_cap));
   ESM_CUDA(cudaMallocHost(&c->h_work128, sizeof(int2) * c->work_cap));
+  ESM_CUDA(cudaMallocHost(&c->h_work256, sizeof(int2) * c->work_cap));
   ESM_CUDA(cudaMallocHost(&c->h_tiles, sizeof(int4) * c->tiles_cap));
   ESM_CUDA(cudaMallocHost(&c->h_moff, sizeof(int64_t) * max_seqs));
   ESM_CUDA(cudaMallocHost(&c->h_roff, sizeof(int64_t) * max_seqs));
@@ -379,7 +388,8 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
             esm::make_tmap_f16(&c->tm_ao, c->ao, rows, d, d, 128) &&
             esm::make_tmap_f16(&c->tm_hb, c->hb, rows, F, F, 128) &&
             esm::make_tmap_f16(&c->tm_qkv_q, c->qkv, rows, 3 * d, 3 * d, 128) &&
-            esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64);
+            esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64) &&
+            esm::make_tmap_f16(&c->tm_qkv_96, c->qkv, rows, 3 * d, 3 * d, 96);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -391,15 +401,22 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
 
 // Builds and uploads the per-call plan (cu_seqlens, attention work list, contact tiles and
 // offsets). Identical consecutive plans are not re-uploaded.
+// The tensor-core contact kernel serves head_dim 64 with up to 64 heads per layer.
+bool use_contact_tc(const esm_ctx* c) {
+  return c->contact_tc && c->cfg.n_heads > 0 && c->cfg.dim / c->cfg.n_heads == 64 && c->cfg.n_heads <= 64;
+}
+
 int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStream_t s) {
   std::vector<int32_t> key(h_cu, h_cu + B + 1);
+  const bool ct = contacts && use_contact_tc(c);
   key.push_back(contacts ? 1 : 0);
+  key.push_back(ct ? 1 : 0);
   if (key == c->plan_key) return ESM_OK;
   const esm_config& g = c->cfg;
   const int64_t hl = static_cast<int64_t>(g.n_layers) * g.n_heads;
   // The previous plan's copies must have left the pinned staging before it is rewritten.
   if (c->plan_ev) ESM_CUDA(cudaEventSynchronize(c->plan_ev));
-  int nw = 0, nw128 = 0, nt = 0;
+  int nw = 0, nw128 = 0, nw256 = 0, nt = 0;
   int64_t moff = 0, roff = 0;
   for (int b = 0; b <= B; ++b) c->h_cu[b] = h_cu[b];
   for (int b = 0; b < B; ++b) {
@@ -408,6 +425,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
     if (nw + qt > c->work_cap) return fail(c, ESM_ECAPACITY, "attention work list exceeds the reserved capacity");
     for (int t = 0; t < qt; ++t) c->h_work[nw++] = make_int2(b, t);
     for (int t = 0; t < (len + 127) / 128; ++t) c->h_work128[nw128++] = make_int2(b, t);
+    for (int t = 0; t < (len + 255) / 256; ++t) c->h_work256[nw256++] = make_int2(b, t);
     if (contacts) {
       const int64_t n = std::max(len - 2, 0);
       c->h_moff[b] = moff;
@@ -415,10 +433,15 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
       moff += n * n;
       roff += hl * n;
       if (n > 0) {
-        if (nt + static_cast<int64_t>(qt) * qt > c->tiles_cap)
-          return fail(c, ESM_ECAPACITY, "contact tiles exceed the reserved capacity");
-        for (int i = 0; i < qt; ++i)
-          for (int j = 0; j < qt; ++j) c->h_tiles[nt++] = make_int4(b, i, j, 0);
+        const int64_t tiles = ct ? esm::contact_tc_tiles(len, nullptr, b) : static_cast<int64_t>(qt) * qt;
+        if (nt + tiles > c->tiles_cap) return fail(c, ESM_ECAPACITY, "contact tiles exceed the reserved capacity");
+        if (ct) {
+          esm::contact_tc_tiles(len, c->h_tiles + nt, b);
+          nt += static_cast<int>(tiles);
+        } else {
+          for (int i = 0; i < qt; ++i)
+            for (int j = 0; j < qt; ++j) c->h_tiles[nt++] = make_int4(b, i, j, 0);
+        }
       }
     }
   }
@@ -427,6 +450,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   ESM_CUDA(cudaMemcpyAsync(c->cu, c->h_cu, sizeof(int32_t) * (B + 1), cudaMemcpyHostToDevice, s));
   ESM_CUDA(cudaMemcpyAsync(c->work, c->h_work, sizeof(int2) * nw, cudaMemcpyHostToDevice, s));
   ESM_CUDA(cudaMemcpyAsync(c->work128, c->h_work128, sizeof(int2) * nw128, cudaMemcpyHostToDevice, s));
+  ESM_CUDA(cudaMemcpyAsync(c->work256, c->h_work256, sizeof(int2) * nw256, cudaMemcpyHostToDevice, s));
   if (contacts) {
     ESM_CUDA(cudaMemcpyAsync(c->m_off, c->h_moff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
     ESM_CUDA(cudaMemcpyAsync(c->r_off, c->h_roff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
@@ -437,6 +461,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   c->plan_key = key;
   c->plan_work = nw;
   c->plan_work128 = nw128;
+  c->plan_work256 = nw256;
   c->plan_tiles = nt;
   return ESM_OK;
 }
@@ -544,10 +569,13 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
-  const bool attn_tc = c->attn_tc && dh == 64;
+  const int attn_tc = dh == 64 ? c->attn_tc : 0;
   esm::AttnParams ap128 = ap;
   ap128.work = c->work128;
   ap128.n_work = c->plan_work128;
+  esm::AttnParams ap256 = ap;
+  ap256.work = c->work256;
+  ap256.n_work = c->plan_work256;
 
   for (int l = 0; l < nl; ++l) {
     esm::LayerSrc src{};
@@ -576,7 +604,9 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
-      if (attn_tc) {
+      if (attn_tc == 2) {
+        ESM_CUDA(esm::launch_attention_tc2(c->tm_qkv_q, c->tm_qkv_kv, ap256, s));
+      } else if (attn_tc) {
         ESM_CUDA(esm::launch_attention_tc(c->tm_qkv_q, c->tm_qkv_kv, ap128, s));
       } else {
         ESM_CUDA(esm::launch_attention(ap, s));
@@ -601,7 +631,12 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       cp.r_off = c->r_off;
       cp.r = c->r;
       cp.head_base = l * H;
-      ESM_CUDA(esm::launch_contact_accumulate(cp, s));
+      cp.err = c->d_err;
+      if (use_contact_tc(c)) {
+        ESM_CUDA(esm::launch_contact_tc(c->tm_qkv_q, c->tm_qkv_96, cp, s));
+      } else {
+        ESM_CUDA(esm::launch_contact_accumulate(cp, s));
+      }
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(dd), 0.0);
@@ -760,7 +795,8 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   c->device = device;
   c->num_sms = prop.multiProcessorCount;
   if (const char* v = std::getenv("ESM_GEMM_CTA_PAIR")) c->cta_pair = std::atoi(v) != 0;
-  if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v) != 0;
+  if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v);
+  if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
     delete c;

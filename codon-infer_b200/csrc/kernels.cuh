@@ -89,6 +89,10 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s);
 // are fp16 tensor maps over qkv [T, 3d] with 64-column boxes of 128 / 64 rows.
 cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
                                 cudaStream_t s);
+// Same with two 128-row query tiles per CTA (attention_tc2.cu): work items are (sequence, 256-row
+// query block).
+cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
+                                 cudaStream_t s);
 
 // Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
 // recomputes P = softmax(q k^T * scale) tile by tile from the saved LSE, adds w * P into the
@@ -108,8 +112,17 @@ struct ContactParams {
   const int64_t* r_off;    // [B] float offset of sequence b's r block ([n_heads_total, n_b])
   float* r;
   int head_base;           // layer * H
+  int* err;                // device error word (bounded waits of the tensor-core kernel)
 };
 cudaError_t launch_contact_accumulate(const ContactParams& p, cudaStream_t s);
+
+// Tensor-core contact accumulation for head_dim 64 (contact_tc.cu): tiles of 128 keys x 96
+// queries, M accumulated transposed. contact_tc_tiles writes sequence b's tile list to `out` (if
+// not null) and returns its length. tm_k128 / tm_q96: qkv [T, 3d] maps with 64-column boxes of 128
+// and 96 rows.
+int contact_tc_tiles(int len, int4* out, int b);
+cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q96, const ContactParams& p,
+                              cudaStream_t s);
 
 // contacts = sigmoid(M + M^T - sum_h a_h r_h r_h^T + b) with a_h = w_h / T_h (APC), per sequence.
 cudaError_t launch_contact_finalize(const float* M, const float* r, const int64_t* m_off, const int64_t* r_off,

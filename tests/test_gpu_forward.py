@@ -188,3 +188,49 @@ def test_device_wait_timeout_reports_and_recovers(esm):
     m.check_device()  # the error word was cleared
     out = m.forward(esm.random_sequences(1, 64))
     assert np.isfinite(out["logits"]).all()
+
+
+def test_650m_shape_contacts_ragged_batch(esm, orc):
+    # head_dim 64 contacts (tensor-core accumulation: 128-key x 96-query tiles, M stored
+    # transposed, row sums from the <cls>/<eos> columns) on sequences that are shorter than one
+    # tile, straddle tile edges, or leave a single inner residue.
+    base = esm.esm2_650m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    m, t, cw = build(esm, cfg, esm.DTYPE_Q4_0)
+    lens = [3, 5, 97, 130, 300, 226]
+    m.reserve(sum(lens), len(lens), 300, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=9)
+    out = m.forward(seqs, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
+
+
+def test_contact_kernels_agree(esm, monkeypatch):
+    # The tensor-core contact kernel and the mma.sync kernel (ESM_CONTACT_TC=0) give the same maps.
+    base = esm.esm2_650m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 3, base.n_heads, arch=base.arch)
+    lens = [64, 250, 389]
+    seqs = esm.random_sequences(len(lens), lens, seed=10)
+    maps = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ESM_CONTACT_TC", flag)
+        m, _, _ = build(esm, cfg, esm.DTYPE_Q8_0, seed=3)
+        m.reserve(sum(lens), len(lens), 389, contacts=True)
+        maps.append(m.forward(seqs, want_contacts=True)["contacts"])
+        m.close()
+    assert np.abs(maps[0] - maps[1]).max() <= 2e-4
+
+
+@pytest.mark.parametrize("attn", ["1", "2"])
+def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn):
+    # Both tcgen05 attention kernels (ESM_ATTN_TC=1: one 128-row query tile per CTA; 2: two tiles
+    # per CTA sharing K/V, P in tensor memory) on lengths at and around the 64-key and 128/256-row
+    # tile edges, with contacts (which read the saved log-sum-exp).
+    monkeypatch.setenv("ESM_ATTN_TC", attn)
+    base = esm.esm2_650m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    m, t, cw = build(esm, cfg, esm.DTYPE_Q4_0, seed=4)
+    lens = [7, 64, 65, 128, 129, 256, 257, 300]
+    m.reserve(sum(lens), len(lens), 300, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=11)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
