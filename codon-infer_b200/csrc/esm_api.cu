@@ -30,8 +30,8 @@ struct esm_ctx {
   int num_sms = 148;
   int cta_pair = 0;  // GEMM tiles on CTA pairs when ESM_GEMM_CTA_PAIR=1 (single CTAs measured faster)
   // Attention kernel for head_dim 64 (ESM_ATTN_TC): 2 = tcgen05, two query tiles per CTA with P in
-  // tensor memory; 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
-  int attn_tc = 1;
+  // tensor memory (measured fastest); 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
+  int attn_tc = 2;
   int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
   std::string err;
