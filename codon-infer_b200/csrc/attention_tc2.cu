@@ -61,6 +61,9 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t kv_addr, int t,
   umma_commit(bar);
 }
 
+// POLY of every 8 column pairs take their exponentials on the FP32 pipe (poly_exp2) instead of the
+// special-function unit, which is the bottleneck of the softmax at head_dim 64.
+template <int POLY>
 __global__ void __launch_bounds__(kThreads2, 2)
     attention_tc2_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
                          const AttnParams p) {
@@ -251,8 +254,11 @@ __global__ void __launch_bounds__(kThreads2, 2)
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float e0 = fast_exp2(fmaf(__uint_as_float(sv[2 * i]), c, -mc));
-            const float e1 = fast_exp2(fmaf(__uint_as_float(sv[2 * i + 1]), c, -mc));
+            const float a0 = fmaf(__uint_as_float(sv[2 * i]), c, -mc);
+            const float a1 = fmaf(__uint_as_float(sv[2 * i + 1]), c, -mc);
+            const bool poly = (i & 7) < POLY;
+            const float e0 = poly ? poly_exp2(a0) : fast_exp2(a0);
+            const float e1 = poly ? poly_exp2(a1) : fast_exp2(a1);
             rs[(2 * i) & 7] += e0;
             rs[(2 * i + 1) & 7] += e1;
             __half2 hv = __floats2half2_rn(e0, e1);
@@ -301,21 +307,34 @@ __global__ void __launch_bounds__(kThreads2, 2)
 
 }  // namespace
 
-cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
-                                 cudaStream_t s) {
-  if (p.n_work <= 0) return cudaSuccess;
-  if (p.dh != kD) return cudaErrorInvalidValue;
+template <int POLY>
+cudaError_t launch_poly(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p, cudaStream_t s) {
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(configured & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
+    cudaError_t e =
+        cudaFuncSetAttribute(attention_tc2_kernel<POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured |= (1ull << dev);
   }
   dim3 grid(p.n_work, p.H);
-  attention_tc2_kernel<<<grid, kThreads2, kSmem2, s>>>(tm_q, tm_kv, p);
+  attention_tc2_kernel<POLY><<<grid, kThreads2, kSmem2, s>>>(tm_q, tm_kv, p);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
+                                 int poly_eighths, cudaStream_t s) {
+  if (p.n_work <= 0) return cudaSuccess;
+  if (p.dh != kD) return cudaErrorInvalidValue;
+  switch (poly_eighths) {
+    case 0: return launch_poly<0>(tm_q, tm_kv, p, s);
+    case 1: return launch_poly<1>(tm_q, tm_kv, p, s);
+    case 2: return launch_poly<2>(tm_q, tm_kv, p, s);
+    case 3: return launch_poly<3>(tm_q, tm_kv, p, s);
+    case 4: return launch_poly<4>(tm_q, tm_kv, p, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace esm

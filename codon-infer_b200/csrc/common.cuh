@@ -223,6 +223,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FP32 pipe, to relieve the special-function unit where exp2 is the bottleneck. Range
+// reduction x = j + f with j = round(x) (add and subtract 1.5 * 2^23, which leaves j in the low
+// mantissa bits of the sum), f in [-0.5, 0.5]; 2^f by a degree-3 polynomial (coefficients: a
+// relative-error least-squares fit of 2^f on Chebyshev nodes of [-0.5, 0.5], refined by
+// reweighting; max relative error 7.5e-5 in fp32 Horner form); 2^j added to the exponent field.
+// Inputs are clamped below at -120, so -inf and very negative arguments give about 7.5e-37
+// instead of 0 (zero after rounding to fp16, negligible in an fp32 sum). Valid for x <= 127.
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -120.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23
+  const float j = t - 12582912.0f;
+  const float f = x - j;
+  float p = fmaf(0.055171605f, f, 0.24261111f);
+  p = fmaf(p, f, 0.69326097f);
+  p = fmaf(p, f, 0.99992806f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -267,12 +285,6 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
-// arrive.expect_tx on the CTA's own barrier for a phase that also counts the peer CTA's bytes.
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
 // TMA load of the pair: data lands in this CTA's shared memory, completion is counted on the
 // mbarrier at shared::cluster address `bar_cluster` (the leader CTA's barrier). No multicast.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,
@@ -311,6 +323,12 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, u
 // pair MMAs issued so far by this thread have completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+// *addr += v (four consecutive fp32, 16-byte aligned) as one vector reduction performed in L2.
+__device__ __forceinline__ void red_add_f32x4(float* addr, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
 }
 

@@ -19,7 +19,7 @@
 // and L-1 add for every query.
 //
 // One CTA per (sequence, 128-key tile, 96-query tile); 320 threads; two CTAs per SM.
-//   warp 0      TMA producer: the K and Q tiles of each contributing head into a 2-stage ring.
+//   warp 0      TMA producer: the K and Q tiles of each contributing head into a 3-stage ring.
 //   warp 1      tcgen05.mma issuer: S^T = K Q^T (M 128, N 96, K 64) into one of two TMEM buffers.
 //   warps 2..9  two warps per TMEM lane quarter, each one key per thread over 48 of the queries:
 //               exp2(S c - lse) on the special-function unit, M^T and column sums in registers; at
@@ -41,7 +41,7 @@ constexpr int kThreadsCt = 320;
 constexpr int kKBytes = kKeys * kD * 2;  // 16 KiB
 constexpr int kQBytes = kQry * kD * 2;   // 12 KiB
 constexpr int kStageBytes = kKBytes + kQBytes;
-constexpr int kStages = 2;
+constexpr int kStages = 3;
 constexpr int kOffLse = kStages * kStageBytes;  // [n_heads][96] lse * log2(e) (inf outside 1..n)
 constexpr int kMaxHeads = 64;
 constexpr int kStageStride = kQry + 1;  // floats per staged M^T row (conflict-free)
@@ -50,7 +50,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // M^T is staged over the operand ring and the log-sum-exp table once the head loop is done.
 inline int contact_tc_smem_bytes(int H) {
-  const int used = kOffLse + H * kQry * 4 + kMaxHeads * 4 + 128;
+  const int used = kOffLse + H * kQry * 4 + kMaxHeads * 8 + 128;
   const int stage = kKeys * kStageStride * 4;
   return (used > stage ? used : stage) + 1024;
 }
@@ -61,15 +61,16 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* lse_s = reinterpret_cast<float*>(smem + kOffLse);
-  int* heads = reinterpret_cast<int*>(smem + kOffLse + p.H * kQry * 4);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffLse + p.H * kQry * 4 + kMaxHeads * 4);
-  uint64_t* full = bars + 0;    // [2]
-  uint64_t* empty = bars + 2;   // [2]
-  uint64_t* s_full = bars + 4;  // [2]
-  uint64_t* s_free = bars + 6;  // [2]
-  uint64_t* drain = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
-  int* nh_s = reinterpret_cast<int*>(bars + 10);
+  int* heads = reinterpret_cast<int*>(smem + kOffLse + p.H * kQry * 4);  // contributing heads
+  float* wts = reinterpret_cast<float*>(heads + kMaxHeads);               // and their weights
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffLse + p.H * kQry * 4 + kMaxHeads * 8);
+  uint64_t* full = bars + 0;    // [3]
+  uint64_t* empty = bars + 3;   // [3]
+  uint64_t* s_full = bars + 6;  // [2]
+  uint64_t* s_free = bars + 8;  // [2]
+  uint64_t* drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  int* nh_s = reinterpret_cast<int*>(bars + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int4 tl = p.tiles[blockIdx.x];
@@ -80,12 +81,19 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
 
   if (threadIdx.x == 0) {
     int nh = 0;
-    for (int h = 0; h < p.H && h < kMaxHeads; ++h)
-      if (p.w_layer[h] != 0.0f) heads[nh++] = h;
+    for (int h = 0; h < p.H && h < kMaxHeads; ++h) {
+      const float w = p.w_layer[h];
+      if (w != 0.0f) {
+        wts[nh] = w;
+        heads[nh++] = h;
+      }
+    }
     *nh_s = nh;
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 8);
     }
@@ -97,10 +105,21 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   if (nh == 0 || n <= 0) return;
   // Row log-sum-exps of this query tile for every contributing head, in the exp2 domain; queries
   // outside the inner block get +inf so that their P is exactly 0.
-  for (int idx = threadIdx.x; idx < nh * kQry; idx += kThreadsCt) {
-    const int t = idx / kQry, c = idx % kQry;
-    const int i = q0 + c;
-    lse_s[idx] = (i >= 1 && i <= n) ? p.lse[static_cast<size_t>(heads[t]) * p.T + start + i] * kLog2e : INFINITY;
+  // All of a thread's loads are issued before the first store, so their latencies overlap.
+  {
+    constexpr int kIters = (kMaxHeads * kQry + kThreadsCt - 1) / kThreadsCt;
+    float lv[kIters];
+#pragma unroll
+    for (int k = 0; k < kIters; ++k) {
+      const int idx = threadIdx.x + k * kThreadsCt;
+      const int t = idx / kQry, i = q0 + idx % kQry;
+      lv[k] = (idx < nh * kQry && i >= 1 && i <= n) ? p.lse[static_cast<size_t>(heads[t]) * p.T + start + i] : INFINITY;
+    }
+#pragma unroll
+    for (int k = 0; k < kIters; ++k) {
+      const int idx = threadIdx.x + k * kThreadsCt;
+      if (idx < nh * kQry) lse_s[idx] = lv[k] * kLog2e;
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -123,8 +142,8 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
       const uint64_t pol = l2_policy_evict_normal();
       int t = 0;
       for (; t < nh; ++t) {
-        const int st = t & 1;
-        if (!mbar_wait(&empty[st], ((t >> 1) & 1) ^ 1u, p.err, kDevTimeoutProducer)) {
+        const int st = t % kStages;
+        if (!mbar_wait(&empty[st], ((t / kStages) & 1) ^ 1u, p.err, kDevTimeoutProducer)) {
           ok = false;
           break;
         }
@@ -135,25 +154,26 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
         tma_load_2d(dst + kKBytes, &tmap_q, &full[st], h * kD, start + q0, pol);
       }
       if (!ok) {  // let the loads already in flight land before the CTA exits
-        for (int tt = (t - 2 > 0 ? t - 2 : 0); tt < t; ++tt)
-          mbar_wait(&full[tt & 1], (tt >> 1) & 1, p.err, kDevTimeoutProducer);
+        for (int tt = (t - kStages > 0 ? t - kStages : 0); tt < t; ++tt)
+          mbar_wait(&full[tt % kStages], (tt / kStages) & 1, p.err, kDevTimeoutProducer);
       }
     }
   } else if (warp == 1) {
     if (elect_one_sync()) {
       constexpr uint32_t idesc = umma_idesc_f16(kKeys, kQry);
       for (int t = 0; t < nh && ok; ++t) {
-        const int st = t & 1;
-        if (!mbar_wait(&full[st], (t >> 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait(&s_free[st], ((t >> 1) - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        const int st = t % kStages;  // operand stage
+        const int sb = t & 1;        // S^T buffer
+        if (!mbar_wait(&full[st], (t / kStages) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (t >= 2 && !mbar_wait(&s_free[sb], ((t >> 1) - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + st * kStageBytes);
         const uint32_t q_addr = k_addr + kKBytes;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k)
-          umma_f16(tmem + st * kSBuf, umma_sdesc_sw128(k_addr + k * 32), umma_sdesc_sw128(q_addr + k * 32), idesc,
+          umma_f16(tmem + sb * kSBuf, umma_sdesc_sw128(k_addr + k * 32), umma_sdesc_sw128(q_addr + k * 32), idesc,
                    k > 0);
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[sb]);
         umma_commit(&empty[st]);
       }
       if (!ok) {
@@ -171,14 +191,14 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
     const bool edge_key = key == 0 || key == len - 1;  // supplies the row-sum term
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float c = p.scale * kLog2e;
+    float* const rbase = p.r + p.r_off[b] + static_cast<size_t>(p.head_base) * n;
     for (int t = 0; t < nh; ++t) {
       const int st = t & 1;
       if (!mbar_wait(&s_full[st], (t >> 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
-      const int h = heads[t];
-      const float w = p.w_layer[h];
+      const float w = wts[t];
       const float* lrow = lse_s + t * kQry + qh * kQHalf;
-      float* rh = p.r + p.r_off[b] + static_cast<size_t>(p.head_base + h) * n;
+      float* rh = rbase + static_cast<size_t>(heads[t]) * n;
       float cs[2] = {0.0f, 0.0f};
 #pragma unroll
       for (int part = 0; part < kQHalf / 16; ++part) {
@@ -196,7 +216,9 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const float lu = u == 0 ? l4.x : u == 1 ? l4.y : u == 2 ? l4.z : l4.w;
-            const float pv = fast_exp2(fmaf(__uint_as_float(s[4 * g + u]), c, -lu));
+            // One exponential in four on the FP32 pipe, the rest on the special-function unit.
+            const float arg = fmaf(__uint_as_float(s[4 * g + u]), c, -lu);
+            const float pv = (u == 3) ? poly_exp2(arg) : fast_exp2(arg);
             cs[u & 1] += pv;
             acc[part * 16 + 4 * g + u] = fmaf(w, pv, acc[part * 16 + 4 * g + u]);
           }
@@ -226,17 +248,33 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   }
   __syncthreads();
   if (!failed && warp >= 2) {
-    // M^T rows of this tile: row (key - 1), columns (q0 + c - 1), inner entries only.
+    // M^T rows of this tile: row (key - 1), columns (q0 + c - 1), inner entries only. Each warp
+    // reads eight of its row segments before writing them, so the loads overlap.
     float* Mb = p.M + p.m_off[b];
     const int wq = warp - 2;
-    for (int rr = wq; rr < kKeys; rr += 8) {
-      const int key = k0 + rr;
-      if (key < 1 || key > n) continue;
-      float* mrow = Mb + static_cast<size_t>(key - 1) * n;
+    constexpr int kBatch = 8, kCols = kQry / 32;
+#pragma unroll 1
+    for (int r0 = 0; r0 < kKeys / 8; r0 += kBatch) {
+      float mv[kBatch][kCols];
 #pragma unroll
-      for (int cc = lane; cc < kQry; cc += 32) {
-        const int i = q0 + cc;
-        if (i >= 1 && i <= n) mrow[i - 1] += stage[rr * kStageStride + cc];
+      for (int k = 0; k < kBatch; ++k) {
+        const int key = k0 + wq + 8 * (r0 + k);
+#pragma unroll
+        for (int u = 0; u < kCols; ++u) {
+          const int i = q0 + lane + 32 * u;
+          mv[k][u] = (key >= 1 && key <= n && i >= 1 && i <= n) ? Mb[static_cast<size_t>(key - 1) * n + (i - 1)] : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int rr = wq + 8 * (r0 + k);
+        const int key = k0 + rr;
+#pragma unroll
+        for (int u = 0; u < kCols; ++u) {
+          const int i = q0 + lane + 32 * u;
+          if (key >= 1 && key <= n && i >= 1 && i <= n)
+            Mb[static_cast<size_t>(key - 1) * n + (i - 1)] = mv[k][u] + stage[rr * kStageStride + lane + 32 * u];
+        }
       }
     }
   }

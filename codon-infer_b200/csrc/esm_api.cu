@@ -28,10 +28,13 @@ struct esm_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
   int num_sms = 148;
-  int cta_pair = 0;  // GEMM tiles on CTA pairs when ESM_GEMM_CTA_PAIR=1 (single CTAs measured faster)
+  int cta_pair = 1;  // GEMM tiles on CTA pairs (cta_group::2); ESM_GEMM_CTA_PAIR=0 selects single CTAs
   // Attention kernel for head_dim 64 (ESM_ATTN_TC): 2 = tcgen05, two query tiles per CTA with P in
   // tensor memory (measured fastest); 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
   int attn_tc = 2;
+  // Eighths of the softmax exponentials on the FP32 pipe (ESM_ATTN_POLY, 0..4); 0 by default, as
+  // moving them measured no faster: the special-function unit is not what bounds that kernel.
+  int attn_poly = 0;
   int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
   std::string err;
@@ -605,7 +608,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
       if (attn_tc == 2) {
-        ESM_CUDA(esm::launch_attention_tc2(c->tm_qkv_q, c->tm_qkv_kv, ap256, s));
+        ESM_CUDA(esm::launch_attention_tc2(c->tm_qkv_q, c->tm_qkv_kv, ap256, c->attn_poly, s));
       } else if (attn_tc) {
         ESM_CUDA(esm::launch_attention_tc(c->tm_qkv_q, c->tm_qkv_kv, ap128, s));
       } else {
@@ -796,6 +799,7 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   c->num_sms = prop.multiProcessorCount;
   if (const char* v = std::getenv("ESM_GEMM_CTA_PAIR")) c->cta_pair = std::atoi(v) != 0;
   if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v);
+  if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(4, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {

@@ -107,30 +107,6 @@ __device__ __forceinline__ void epi16(const GemmParams& p, int m, int n, const u
   }
 }
 
-// Residual update x[m, n..n+16) += acc + bias; the current x values are requested before the
-// tensor-memory load is waited for, so both latencies overlap.
-__device__ __forceinline__ void resid16_load(const GemmParams& p, int m, int n, float4 (&x)[4]) {
-  const float4* src =
-      reinterpret_cast<const float4*>(static_cast<const float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = src[i];
-}
-__device__ __forceinline__ void resid16_store(const GemmParams& p, int m, int n, const uint32_t* r,
-                                              const float4 (&x)[4]) {
-  float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
-  const float4* b4 = reinterpret_cast<const float4*>(p.bias + n);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 b = p.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 o = x[i];
-    o.x += __uint_as_float(r[4 * i + 0]) + b.x;
-    o.y += __uint_as_float(r[4 * i + 1]) + b.y;
-    o.z += __uint_as_float(r[4 * i + 2]) + b.z;
-    o.w += __uint_as_float(r[4 * i + 3]) + b.w;
-    dst[i] = o;
-  }
-}
-
 template <int BN, int EPI, int DH, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -210,7 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           if constexpr (CG == 2) {
-            if (rank == 0) mbar_arrive_expect_tx_cluster(&full[stage], 2 * S::kStageBytes);
+            // The leader's own arrive needs no cluster-scope release: the peer's bytes reach this
+            // barrier through its TMA's complete_tx, and a per-stage cluster fence in this single
+            // producer thread would throttle the whole pipeline.
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
             const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
             tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBK, a_row, pol_a);
             tma_load_2d_pair(sb, &tmap_b, leader_full, kb * kBK, b_row, pol_b);
@@ -420,14 +399,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if constexpr (EPI == kEpiResidF32) {
+        // x += acc + bias as vector reductions performed in L2: the residual stream is never
+        // read into the SM, so the epilogue issues its stores without waiting on loads.
 #pragma unroll 1
         for (int c = c_begin; c < c_end; c += 16) {
-          float4 x[4];
-          if (row_ok) resid16_load(p, m, n0 + c, x);
+          float4 b[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            b[i] = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + n0 + c) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
           uint32_t r[16];
           tmem_ld16(t_row + c, r);
           tmem_ld_wait();
-          if (row_ok) resid16_store(p, m, n0 + c, r, x);
+          if (row_ok) {
+            float* dst = static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n0 + c;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              red_add_f32x4(dst + 4 * i, make_float4(__uint_as_float(r[4 * i + 0]) + b[i].x,
+                                                      __uint_as_float(r[4 * i + 1]) + b[i].y,
+                                                      __uint_as_float(r[4 * i + 2]) + b[i].z,
+                                                      __uint_as_float(r[4 * i + 3]) + b[i].w));
+          }
         }
       } else {
         int c = c_begin;

@@ -90,9 +90,9 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s);
 cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
                                 cudaStream_t s);
 // Same with two 128-row query tiles per CTA (attention_tc2.cu): work items are (sequence, 256-row
-// query block).
+// query block); poly_eighths (0..4) of the softmax exponentials are computed on the FP32 pipe.
 cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
-                                 cudaStream_t s);
+                                 int poly_eighths, cudaStream_t s);
 
 // Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
 // recomputes P = softmax(q k^T * scale) tile by tile from the saved LSE, adds w * P into the

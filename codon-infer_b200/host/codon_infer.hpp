@@ -182,7 +182,9 @@ class DeviceWeights {
   // here: n_layers * n_heads weights (layer-major) and the bias.
   void set_contact_head(const std::vector<float>& weights, float bias) {
     check(esm_set_contact_head(ctx_, weights.data(), static_cast<int32_t>(weights.size()), bias));
+    has_contact_head_ = true;
   }
+  bool has_contact_head() const { return has_contact_head_; }
   void check(int rc) const {
     if (rc == ESM_OK) return;
     const std::string msg = esm_last_error(ctx_);
@@ -201,6 +203,7 @@ class DeviceWeights {
   esm_ctx* ctx_ = nullptr;
   size_t reserved_len_ = 0;
   bool reserved_contacts_ = false;
+  bool has_contact_head_ = false;
 
   void load_file(const std::string& path) {
     const esm_config c = cfg_.to_c();
@@ -263,7 +266,8 @@ inline void run(const std::vector<size_t>& tokens, DeviceWeights& w, Bidirection
     throw std::logic_error("Sequence length " + std::to_string(L) + " exceeds max_len " +
                            std::to_string(state.max_len));
   const size_t n = L >= 2 ? L - 2 : 0;
-  const bool contacts = state.compute_contacts && n > 0;
+  // Contact maps need the regression head (an input here, set with set_contact_head).
+  const bool contacts = state.compute_contacts && n > 0 && w.has_contact_head();
   if (w.reserved_len() < state.max_len || (contacts && !w.reserved_contacts())) w.reserve(state.max_len, contacts);
   std::vector<int32_t> toks(tokens.begin(), tokens.end());
   const int32_t len = static_cast<int32_t>(L);
