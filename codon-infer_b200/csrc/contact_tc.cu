@@ -10,20 +10,22 @@
 // log-sum-exp that the attention kernel saved, so no per-head map is stored.
 //
 // The tile is computed transposed: S^T = K Q^T with M = 128 keys (tensor-memory lanes, one key per
-// thread) and N = 96 queries. A thread then owns a key column of P: its column sum accumulates in
-// a register, and it keeps 48 entries of M^T for its key in registers across all heads (96
-// queries keep the 48 accumulators, the S^T chunk and the addressing within 96 registers, the
-// limit for two 320-thread CTAs per SM). M is only ever used as M + M^T, so storing M^T in place
-// of M gives the same contacts. The row sums need no reduction: rows of P sum to one over all L
+// thread) and N = 64 queries. A thread then owns a key column of P: its column sum accumulates in
+// a register, and it keeps 32 entries of M^T for its key in registers across all heads. M is only
+// ever used as M + M^T, so storing M^T in place of M gives the same contacts. The row sums need no reduction: rows of P sum to one over all L
 // keys, so rowsum over the inner keys is 1 - P[i, 0] - P[i, L-1], which the threads owning keys 0
 // and L-1 add for every query.
 //
-// One CTA per (sequence, 128-key tile, 96-query tile); 320 threads; two CTAs per SM.
-//   warp 0      TMA producer: the K and Q tiles of each contributing head into a 3-stage ring.
-//   warp 1      tcgen05.mma issuer: S^T = K Q^T (M 128, N 96, K 64) into one of two TMEM buffers.
-//   warps 2..9  two warps per TMEM lane quarter, each one key per thread over 48 of the queries:
-//               exp2(S c - lse) on the special-function unit, M^T and column sums in registers; at
-//               the end M^T is staged through shared memory and added to M with coalesced rows.
+// One CTA per (sequence, 128-key tile, 64-query tile); 320 threads; two CTAs per SM.
+//   warp 0      TMA producer: the K and Q tiles of each contributing head into a 4-stage ring.
+//   warp 1      tcgen05.mma issuer: S^T = K Q^T (M 128, N 64, K 64) into one of four TMEM buffers.
+//   warps 2..9  two warps per TMEM lane quarter, each one key per thread over 32 of the queries:
+//               copy its S^T slice to registers and release the buffer at once, then exp2(S c - lse)
+//               (three in four on the special-function unit, one on the FP32 pipe), M^T and column
+//               sums in registers; at the end M^T is staged through shared memory and added to M
+//               with coalesced rows.
+// Four S^T buffers let the MMAs run up to three heads ahead of the exponentials: with two, the
+// round trip MMA -> softmax read -> buffer release -> next MMA set the pace, not the math.
 // All waits are bounded; on a timeout the error word is set and M is left untouched.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -33,24 +35,24 @@ namespace esm {
 namespace {
 
 constexpr int kKeys = 128;    // keys per tile (MMA M, TMEM lanes)
-constexpr int kQry = 96;      // queries per tile (MMA N)
-constexpr int kQHalf = 48;    // queries per epilogue thread
-constexpr int kSBuf = 128;    // TMEM columns between the two S^T buffers
+constexpr int kQry = 64;      // queries per tile (MMA N)
+constexpr int kQHalf = 32;    // queries per epilogue thread
+constexpr int kSBufs = 4;     // S^T buffers in tensor memory (64 columns each)
 constexpr int kD = 64;        // head dim (MMA K)
 constexpr int kThreadsCt = 320;
 constexpr int kKBytes = kKeys * kD * 2;  // 16 KiB
-constexpr int kQBytes = kQry * kD * 2;   // 12 KiB
+constexpr int kQBytes = kQry * kD * 2;   // 8 KiB
 constexpr int kStageBytes = kKBytes + kQBytes;
-constexpr int kStages = 3;
-constexpr int kOffLse = kStages * kStageBytes;  // [n_heads][96] lse * log2(e) (inf outside 1..n)
+constexpr int kStages = 4;
+constexpr int kOffLse = kStages * kStageBytes;  // [n_heads][64] lse * log2(e) (inf outside 1..n)
 constexpr int kMaxHeads = 64;
 constexpr int kStageStride = kQry + 1;  // floats per staged M^T row (conflict-free)
-constexpr uint32_t kTmemCols = 256;     // two S^T buffers of 96 columns, 128 apart
+constexpr uint32_t kTmemCols = 256;     // four S^T buffers of 64 columns
 constexpr float kLog2e = 1.4426950408889634f;
 
 // M^T is staged over the operand ring and the log-sum-exp table once the head loop is done.
 inline int contact_tc_smem_bytes(int H) {
-  const int used = kOffLse + H * kQry * 4 + kMaxHeads * 8 + 128;
+  const int used = kOffLse + H * kQry * 4 + kMaxHeads * 8 + 256;
   const int stage = kKeys * kStageStride * 4;
   return (used > stage ? used : stage) + 1024;
 }
@@ -64,13 +66,13 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   int* heads = reinterpret_cast<int*>(smem + kOffLse + p.H * kQry * 4);  // contributing heads
   float* wts = reinterpret_cast<float*>(heads + kMaxHeads);               // and their weights
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffLse + p.H * kQry * 4 + kMaxHeads * 8);
-  uint64_t* full = bars + 0;    // [3]
-  uint64_t* empty = bars + 3;   // [3]
-  uint64_t* s_full = bars + 6;  // [2]
-  uint64_t* s_free = bars + 8;  // [2]
-  uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
-  int* nh_s = reinterpret_cast<int*>(bars + 12);
+  uint64_t* full = bars + 0;                       // [kStages]
+  uint64_t* empty = full + kStages;                // [kStages]
+  uint64_t* s_full = empty + kStages;              // [kSBufs]
+  uint64_t* s_free = s_full + kSBufs;              // [kSBufs]
+  uint64_t* drain = s_free + kSBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* nh_s = reinterpret_cast<int*>(drain + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int4 tl = p.tiles[blockIdx.x];
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kSBufs; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 8);
     }
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  float acc[kQHalf];  // M^T[key, q0 + 48 * qh + c] summed over heads (epilogue threads)
+  float acc[kQHalf];  // M^T[key, q0 + 32 * qh + c] summed over heads (epilogue threads)
 #pragma unroll
   for (int c = 0; c < kQHalf; ++c) acc[c] = 0.0f;
   bool ok = true;
@@ -139,7 +141,9 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
     if (elect_one_sync()) {
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_q);
-      const uint64_t pol = l2_policy_evict_normal();
+      // Q and K of a layer are re-read by every tile of the sequence: keep them in L2 ahead of the
+      // M accumulator, which streams through once per layer.
+      const uint64_t pol = l2_policy_evict_last();
       int t = 0;
       for (; t < nh; ++t) {
         const int st = t % kStages;
@@ -163,15 +167,18 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
       constexpr uint32_t idesc = umma_idesc_f16(kKeys, kQry);
       for (int t = 0; t < nh && ok; ++t) {
         const int st = t % kStages;  // operand stage
-        const int sb = t & 1;        // S^T buffer
+        const int sb = t % kSBufs;   // S^T buffer
         if (!mbar_wait(&full[st], (t / kStages) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait(&s_free[sb], ((t >> 1) - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (t >= kSBufs && !mbar_wait(&s_free[sb], ((t / kSBufs) - 1) & 1, p.err, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + st * kStageBytes);
         const uint32_t q_addr = k_addr + kKBytes;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k)
-          umma_f16(tmem + sb * kSBuf, umma_sdesc_sw128(k_addr + k * 32), umma_sdesc_sw128(q_addr + k * 32), idesc,
+          umma_f16(tmem + sb * kQry, umma_sdesc_sw128(k_addr + k * 32), umma_sdesc_sw128(q_addr + k * 32), idesc,
                    k > 0);
         umma_commit(&s_full[sb]);
         umma_commit(&empty[st]);
@@ -182,9 +189,9 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
       }
     }
   } else {
-    // ---------------- one key per thread, 48 queries per warp ----------------
+    // ---------------- one key per thread, 32 queries per warp ----------------
     const int quarter = warp & 3;
-    const int qh = (warp - 2) >> 2;      // which 48 queries of the tile
+    const int qh = (warp - 2) >> 2;      // which 32 queries of the tile
     const int kr = quarter * 32 + lane;  // key row inside the tile = TMEM lane
     const int key = k0 + kr;             // token index inside the sequence
     const bool inner_key = key >= 1 && key <= n;
@@ -193,45 +200,40 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
     const float c = p.scale * kLog2e;
     float* const rbase = p.r + p.r_off[b] + static_cast<size_t>(p.head_base) * n;
     for (int t = 0; t < nh; ++t) {
-      const int st = t & 1;
-      if (!mbar_wait(&s_full[st], (t >> 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      const int sb = t % kSBufs;
+      if (!mbar_wait(&s_full[sb], (t / kSBufs) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
+      uint32_t s[kQHalf];
+      tmem_ld32(tmem + sb * kQry + lane_off + qh * kQHalf, s);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);  // the MMA of head t + 4 may overwrite this buffer
       const float w = wts[t];
       const float* lrow = lse_s + t * kQry + qh * kQHalf;
       float* rh = rbase + static_cast<size_t>(heads[t]) * n;
       float cs[2] = {0.0f, 0.0f};
 #pragma unroll
-      for (int part = 0; part < kQHalf / 16; ++part) {
-        uint32_t s[16];
-        tmem_ld16(tmem + st * kSBuf + lane_off + qh * kQHalf + part * 16, s);
-        tmem_ld_wait();
-        if (part == kQHalf / 16 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[st]);  // the MMA of head t + 2 may overwrite this buffer
+      for (int g = 0; g < kQHalf / 4; ++g) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lrow + 4 * g);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float lu = u == 0 ? l4.x : u == 1 ? l4.y : u == 2 ? l4.z : l4.w;
+          // One exponential in four on the FP32 pipe, the rest on the special-function unit.
+          const float arg = fmaf(__uint_as_float(s[4 * g + u]), c, -lu);
+          const float pv = (u == 3) ? poly_exp2(arg) : fast_exp2(arg);
+          cs[u & 1] += pv;
+          acc[4 * g + u] = fmaf(w, pv, acc[4 * g + u]);
         }
+      }
+      if (edge_key) {
+        // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i.
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const float4 l4 = *reinterpret_cast<const float4*>(lrow + part * 16 + 4 * g);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float lu = u == 0 ? l4.x : u == 1 ? l4.y : u == 2 ? l4.z : l4.w;
-            // One exponential in four on the FP32 pipe, the rest on the special-function unit.
-            const float arg = fmaf(__uint_as_float(s[4 * g + u]), c, -lu);
-            const float pv = (u == 3) ? poly_exp2(arg) : fast_exp2(arg);
-            cs[u & 1] += pv;
-            acc[part * 16 + 4 * g + u] = fmaf(w, pv, acc[part * 16 + 4 * g + u]);
-          }
-        }
-        if (edge_key) {
-          // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i.
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int i = q0 + qh * kQHalf + part * 16 + u;
-            if (i < 1 || i > n) continue;
-            const float pv = fast_exp2(fmaf(__uint_as_float(s[u]), c, -lrow[part * 16 + u]));
-            atomicAdd(rh + (i - 1), (key == 0 ? 1.0f : 0.0f) - pv);
-          }
+        for (int u = 0; u < kQHalf; ++u) {
+          const int i = q0 + qh * kQHalf + u;
+          if (i < 1 || i > n) continue;
+          const float pv = fast_exp2(fmaf(__uint_as_float(s[u]), c, -lrow[u]));
+          atomicAdd(rh + (i - 1), (key == 0 ? 1.0f : 0.0f) - pv);
         }
       }
       if (inner_key) atomicAdd(rh + (key - 1), cs[0] + cs[1]);
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
 #pragma unroll
         for (int u = 0; u < kCols; ++u) {
           const int i = q0 + lane + 32 * u;
-          mv[k][u] = (key >= 1 && key <= n && i >= 1 && i <= n) ? Mb[static_cast<size_t>(key - 1) * n + (i - 1)] : 0.0f;
+          mv[k][u] = (key >= 1 && key <= n && i >= 1 && i <= n) ? __ldcs(Mb + static_cast<size_t>(key - 1) * n + (i - 1)) : 0.0f;
         }
       }
 #pragma unroll
@@ -273,7 +275,7 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
         for (int u = 0; u < kCols; ++u) {
           const int i = q0 + lane + 32 * u;
           if (key >= 1 && key <= n && i >= 1 && i <= n)
-            Mb[static_cast<size_t>(key - 1) * n + (i - 1)] = mv[k][u] + stage[rr * kStageStride + lane + 32 * u];
+            __stcs(Mb + static_cast<size_t>(key - 1) * n + (i - 1), mv[k][u] + stage[rr * kStageStride + lane + 32 * u]);
         }
       }
     }
@@ -294,7 +296,7 @@ int contact_tc_tiles(int len, int4* out, int b) {
   return kt * qt;
 }
 
-cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q96, const ContactParams& p,
+cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q64, const ContactParams& p,
                               cudaStream_t s) {
   if (p.n_tiles <= 0) return cudaSuccess;
   if (p.dh != kD || p.H > kMaxHeads) return cudaErrorInvalidValue;
@@ -309,7 +311,7 @@ cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_
     if (e != cudaSuccess) return e;
     if (dev < 64) configured |= (1ull << dev);
   }
-  contact_tc_kernel<<<p.n_tiles, kThreadsCt, smem, s>>>(tm_k128, tm_q96, p);
+  contact_tc_kernel<<<p.n_tiles, kThreadsCt, smem, s>>>(tm_k128, tm_q64, p);
   return cudaGetLastError();
 }
 

@@ -94,7 +94,7 @@ struct esm_ctx {
   float* a_scr = nullptr;
   float* cmap = nullptr;
   CUtensorMap tm_xn, tm_ao, tm_hb;
-  CUtensorMap tm_qkv_q, tm_qkv_kv, tm_qkv_96;  // qkv [T, 3d] with 64-column boxes of 128 / 64 / 96 rows
+  CUtensorMap tm_qkv_q, tm_qkv_kv;  // qkv [T, 3d] with 64-column boxes of 128 / 64 rows
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
@@ -391,8 +391,7 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
             esm::make_tmap_f16(&c->tm_ao, c->ao, rows, d, d, 128) &&
             esm::make_tmap_f16(&c->tm_hb, c->hb, rows, F, F, 128) &&
             esm::make_tmap_f16(&c->tm_qkv_q, c->qkv, rows, 3 * d, 3 * d, 128) &&
-            esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64) &&
-            esm::make_tmap_f16(&c->tm_qkv_96, c->qkv, rows, 3 * d, 3 * d, 96);
+            esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -580,6 +579,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap256.work = c->work256;
   ap256.n_work = c->plan_work256;
 
+
   for (int l = 0; l < nl; ++l) {
     esm::LayerSrc src{};
     src.dtype = c->dtype;
@@ -636,7 +636,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       cp.head_base = l * H;
       cp.err = c->d_err;
       if (use_contact_tc(c)) {
-        ESM_CUDA(esm::launch_contact_tc(c->tm_qkv_q, c->tm_qkv_96, cp, s));
+        ESM_CUDA(esm::launch_contact_tc(c->tm_qkv_q, c->tm_qkv_kv, cp, s));
       } else {
         ESM_CUDA(esm::launch_contact_accumulate(cp, s));
       }

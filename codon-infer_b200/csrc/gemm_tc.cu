@@ -32,7 +32,7 @@ namespace {
 constexpr int kBK = 64;  // one 128-byte swizzle span of fp16
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemBudget = 224 * 1024;  // operand ring; 7 stages of 32 KiB for CTA-pair tiles
 
 template <int BN, int CG>
 struct GemmShape {

@@ -116,12 +116,12 @@ struct ContactParams {
 };
 cudaError_t launch_contact_accumulate(const ContactParams& p, cudaStream_t s);
 
-// Tensor-core contact accumulation for head_dim 64 (contact_tc.cu): tiles of 128 keys x 96
+// Tensor-core contact accumulation for head_dim 64 (contact_tc.cu): tiles of 128 keys x 64
 // queries, M accumulated transposed. contact_tc_tiles writes sequence b's tile list to `out` (if
-// not null) and returns its length. tm_k128 / tm_q96: qkv [T, 3d] maps with 64-column boxes of 128
-// and 96 rows.
+// not null) and returns its length. tm_k128 / tm_q64: qkv [T, 3d] maps with 64-column boxes of 128
+// and 64 rows.
 int contact_tc_tiles(int len, int4* out, int b);
-cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q96, const ContactParams& p,
+cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q64, const ContactParams& p,
                               cudaStream_t s);
 
 // contacts = sigmoid(M + M^T - sum_h a_h r_h r_h^T + b) with a_h = w_h / T_h (APC), per sequence.

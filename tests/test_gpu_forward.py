@@ -239,8 +239,8 @@ def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly):
     base = esm.esm2_650m()
     cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
     m, t, cw = build(esm, cfg, esm.DTYPE_Q4_0, seed=4)
-    lens = [7, 64, 65, 128, 129, 256, 257, 300]
-    m.reserve(sum(lens), len(lens), 300, contacts=True)
+    lens = [7, 64, 65, 128, 129, 256, 257, 300, 513, 640]
+    m.reserve(sum(lens), len(lens), 640, contacts=True)
     seqs = esm.random_sequences(len(lens), lens, seed=11)
     out = m.forward(seqs, want_hidden=True, want_contacts=True)
     compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
