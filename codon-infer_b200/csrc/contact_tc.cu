@@ -81,16 +81,30 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   const int len = p.cu_seqlens[b + 1] - start;
   const int n = len - 2;
 
-  if (threadIdx.x == 0) {
-    int nh = 0;
-    for (int h = 0; h < p.H && h < kMaxHeads; ++h) {
-      const float w = p.w_layer[h];
-      if (w != 0.0f) {
-        wts[nh] = w;
-        heads[nh++] = h;
-      }
+  if (warp == 0) {
+    // Heads with a non-zero weight (H <= 64), compacted with ballots. Each CTA starts its head loop
+    // at a different head, so the CTAs running at the same time do not all fetch the same K and Q
+    // lines from L2 at once.
+    const float w0 = lane < p.H ? p.w_layer[lane] : 0.0f;
+    const float w1 = lane + 32 < p.H ? p.w_layer[lane + 32] : 0.0f;
+    const unsigned m0 = __ballot_sync(0xffffffffu, w0 != 0.0f);
+    const unsigned m1 = __ballot_sync(0xffffffffu, w1 != 0.0f);
+    const int n0 = __popc(m0), nh = n0 + __popc(m1);
+    const int rot = nh > 0 ? static_cast<int>(blockIdx.x % nh) : 0;
+    const unsigned below = (1u << lane) - 1u;
+    if (w0 != 0.0f) {
+      const int slot = (__popc(m0 & below) - rot + nh) % nh;
+      heads[slot] = lane;
+      wts[slot] = w0;
     }
-    *nh_s = nh;
+    if (w1 != 0.0f) {
+      const int slot = (n0 + __popc(m1 & below) - rot + nh) % nh;
+      heads[slot] = lane + 32;
+      wts[slot] = w1;
+    }
+    if (lane == 0) *nh_s = nh;
+  }
+  if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);

@@ -468,8 +468,8 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   return ESM_OK;
 }
 
-int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int M, int N, int K,
-         const float* bias, void* out, int ldo, cudaStream_t s) {
+int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, int bn, int epi, int M,
+         int N, int K, const float* bias, void* out, int ldo, cudaStream_t s) {
   esm::GemmParams p{};
   p.M = M;
   p.N = N;
@@ -482,7 +482,7 @@ int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, int bn, int e
   p.rope_cols = 2 * c->cfg.dim;
   p.err = c->d_err;
   const int dh = c->cfg.dim / c->cfg.n_heads;
-  ESM_CUDA(esm::gemm_launch(ta, tb, bn, epi, epi == esm::kEpiQkvRope ? dh : 0, p, c->num_sms, s, c->cta_pair));
+  ESM_CUDA(esm::gemm_launch(ta, tb, tout, bn, epi, epi == esm::kEpiQkvRope ? dh : 0, p, c->num_sms, s, c->cta_pair));
   return ESM_OK;
 }
 
@@ -558,6 +558,17 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     ESM_CUDA(cudaMemsetAsync(c->r, 0, std::max<int64_t>(r_total, 1) * 4, s));
   }
 
+  // Output maps of the bulk-store GEMM epilogues, over exactly this call's T rows (rows past T of a
+  // 32-row block are clipped by the map, not written).
+  CUtensorMap tm_out_qkv, tm_out_hb, tm_out_x;
+  const bool out_maps = esm::make_tmap_out(&tm_out_qkv, c->qkv, 2, T, 3 * d, 3 * d) &&
+                        esm::make_tmap_out(&tm_out_hb, c->hb, 2, T, F, F) &&
+                        esm::make_tmap_out(&tm_out_x, c->x, 4, T, d, d);
+  if (!out_maps) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for a GEMM output");
+  const CUtensorMap* out_qkv = &tm_out_qkv;
+  const CUtensorMap* out_hb = &tm_out_hb;
+  const CUtensorMap* out_x = &tm_out_x;
+
   esm::AttnParams ap{};
   ap.qkv = c->qkv;
   ap.out = c->ao;
@@ -601,7 +612,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * 3.0 * d * d, 0.0);
-      rc = gemm(c, c->tm_xn, c->tm_wqkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d,
+      rc = gemm(c, c->tm_xn, c->tm_wqkv, out_qkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d,
                 c->bqkv + static_cast<int64_t>(l) * 3 * d, c->qkv, 3 * d, s);
       if (rc) return rc;
     }
@@ -643,7 +654,8 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(dd), 0.0);
-      rc = gemm(c, c->tm_ao, c->tm_wo, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d, s);
+      rc = gemm(c, c->tm_ao, c->tm_wo, out_x, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d,
+                s);
       if (rc) return rc;
     }
     {
@@ -652,13 +664,13 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(fd), 0.0);
-      rc = gemm(c, c->tm_xn, c->tm_w1, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb,
+      rc = gemm(c, c->tm_xn, c->tm_w1, out_hb, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb,
                 F, s);
       if (rc) return rc;
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(fd), 0.0);
-      rc = gemm(c, c->tm_hb, c->tm_w2, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x,
+      rc = gemm(c, c->tm_hb, c->tm_w2, out_x, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x,
                 d, s);
       if (rc) return rc;
     }
@@ -690,7 +702,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     const float* dec_b = dec_w + static_cast<int64_t>(V) * d;
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(dd), 0.0);
-      rc = gemm(c, c->tm_xn, c->tm_dense, c->bn_dense, esm::kEpiGeluF32, T, d, d, dense_b, c->headf, d, s);
+      rc = gemm(c, c->tm_xn, c->tm_dense, nullptr, c->bn_dense, esm::kEpiGeluF32, T, d, d, dense_b, c->headf, d, s);
       if (rc) return rc;
     }
     ProfScope ps(c, s, ESM_PROF_HEAD, 2.0 * T * static_cast<double>(V) * d, rowb * 4.0);
@@ -1190,7 +1202,7 @@ int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, c
   p.out = o32;
   p.ldo = n_pad;
   p.err = c->d_err;
-  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, c->num_sms, s, c->cta_pair);
+  e = esm::gemm_launch(ta, tb, nullptr, bn, esm::kEpiStoreF32, 0, p, c->num_sms, s, c->cta_pair);
   if (e == cudaSuccess)
     e = cudaMemcpy2DAsync(out, static_cast<size_t>(out_dim) * 4, o32, static_cast<size_t>(n_pad) * 4,
                           static_cast<size_t>(out_dim) * 4, seq_len, cudaMemcpyDeviceToHost, s);

@@ -32,20 +32,25 @@ namespace {
 constexpr int kBK = 64;  // one 128-byte swizzle span of fp16
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kSmemBudget = 224 * 1024;  // operand ring; 7 stages of 32 KiB for CTA-pair tiles
+constexpr int kSmemBudget = 224 * 1024;  // operand ring + epilogue staging
+constexpr int kStageChunk = 2048;         // one epilogue staging block: 32 rows x 64 bytes
 
-template <int BN, int CG>
+template <int BN, int CG, bool TS>
 struct GemmShape {
   static constexpr int kRows = 128;          // accumulator rows per CTA
   static constexpr int kBRows = BN / CG;     // B rows staged per CTA
   static constexpr int kABytes = kRows * kBK * 2;
   static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
+  // Bulk-store epilogues keep two staging blocks per epilogue warp after the operand ring.
+  static constexpr int kStagingBytes = TS ? kEpiWarps * 2 * kStageChunk : 0;
+  static constexpr int kRing = kSmemBudget - kStagingBytes;
+  static constexpr int kStages = (kRing / kStageBytes) > 8 ? 8 : (kRing / kStageBytes);
+  static constexpr int kOffStaging = kStages * kStageBytes;
   static constexpr int kAccStride = BN <= 128 ? 128 : 256;  // TMEM columns between the two accumulators
   static constexpr int kTmemCols = 2 * kAccStride;
   static constexpr int kBarrierBytes = (2 * kStages + 5) * 8 + 16;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // +1024 for alignment
+  static constexpr int kSmemBytes = kOffStaging + kStagingBytes + kBarrierBytes + 1024;  // +1024 for alignment
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N is a multiple of 16 in [16, 256]");
   static_assert((BN / 2) % 8 == 0, "B half tiles must keep stages 1024-byte aligned");
   static_assert(kStages >= 2, "need at least two stages");
@@ -107,14 +112,22 @@ __device__ __forceinline__ void epi16(const GemmParams& p, int m, int n, const u
   }
 }
 
-template <int BN, int EPI, int DH, int CG>
+// Writes one thread's 64-byte row segment (four 16-byte pieces) into a 32-row staging block laid
+// out for a tensor map with 64-byte swizzle: piece c of row r sits at piece c ^ ((r >> 1) & 3).
+__device__ __forceinline__ void stage_row64(uint8_t* blk, int r, const uint4* v) {
+  const int sw = (r >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(blk + r * 64 + ((c ^ sw) << 4)) = v[c];
+}
+
+template <int BN, int EPI, int DH, int CG, bool TS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const GemmParams p) {
-  using S = GemmShape<BN, CG>;
+                   const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
+  using S = GemmShape<BN, CG, TS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kOffStaging + S::kStagingBytes);
   uint64_t* empty = full + S::kStages;
   uint64_t* acc_full = empty + S::kStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -296,6 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t leader_acc_empty0 =
         (CG == 2) ? mapa_shared(smem_u32(&acc_empty[0]), 0) : smem_u32(&acc_empty[0]);
     int local = 0;
+    int sbuf = 0;  // staging block of the next bulk store (bulk-store epilogues)
+    (void)sbuf;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
       const int m_blk = tile / p.num_n_blocks;
       const int n_blk = tile - m_blk * p.num_n_blocks;
@@ -309,7 +324,165 @@ __global__ void __launch_bounds__(kThreads, 1)
                              static_cast<uint32_t>(buf * S::kAccStride);
       const int n0 = n_blk * BN;
 
-      if constexpr (EPI == kEpiQkvRope && (DH / 2) % 16 == 0) {
+      if constexpr (TS) {
+        // Bulk-store epilogue: each warp writes 32-row x 64-byte blocks of its rows into a
+        // swizzled staging block and one lane stores (or, for the residual, reduce-adds) the block
+        // with the tensor map. Rows past M are clipped by the map.
+        uint8_t* stg = smem + S::kOffStaging + (warp - 2) * (2 * kStageChunk);
+        const int row0 = m_blk * (128 * CG) + 128 * static_cast<int>(rank) + quarter * 32;
+        if constexpr (EPI == kEpiQkvRope) {
+          constexpr int HALF = DH / 2;  // 32 or 16
+          const int pos = row_ok ? __ldg(p.pos + m) : 0;
+          float4 cs_all[HALF / 2];
+          if (n0 + c_begin < p.rope_cols) {
+            const float4* cs_row = reinterpret_cast<const float4*>(p.rope + static_cast<size_t>(pos) * HALF);
+#pragma unroll
+            for (int i = 0; i < HALF / 2; ++i) cs_all[i] = __ldg(cs_row + i);
+          }
+#pragma unroll 1
+          for (int c = c_begin; c < c_end; c += DH) {
+            const int n = n0 + c;
+            if (lane == 0) bulk_wait_read<0>();  // both staging blocks are free again
+            __syncwarp();
+            if (n < p.rope_cols) {
+              // DH 64: block 0 = rotated first half (columns [0, 32)), block 1 = second half.
+              // DH 32: one block, the 16 first-half columns then the 16 second-half columns.
+#pragma unroll
+              for (int sub = 0; sub < HALF; sub += 16) {
+                float4 b0[4], b1[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  b0[i] = __ldg(reinterpret_cast<const float4*>(p.bias + n + sub) + i);
+                  b1[i] = __ldg(reinterpret_cast<const float4*>(p.bias + n + HALF + sub) + i);
+                }
+                const float4* cs = cs_all + sub / 2;
+                uint32_t r0[16], r1[16];
+                tmem_ld16(t_row + c + sub, r0);
+                tmem_ld16(t_row + c + HALF + sub, r1);
+                tmem_ld_wait();
+                const float* bb0 = reinterpret_cast<const float*>(b0);
+                const float* bb1 = reinterpret_cast<const float*>(b1);
+                const float* cc = reinterpret_cast<const float*>(cs);
+                __half2 h0[8], h1[8];
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                  const float x0a = __uint_as_float(r0[j]) + bb0[j], x0b = __uint_as_float(r0[j + 1]) + bb0[j + 1];
+                  const float x1a = __uint_as_float(r1[j]) + bb1[j], x1b = __uint_as_float(r1[j + 1]) + bb1[j + 1];
+                  h0[j / 2] = __floats2half2_rn(x0a * cc[2 * j] - x1a * cc[2 * j + 1],
+                                                x0b * cc[2 * j + 2] - x1b * cc[2 * j + 3]);
+                  h1[j / 2] = __floats2half2_rn(x1a * cc[2 * j] + x0a * cc[2 * j + 1],
+                                                x1b * cc[2 * j + 2] + x0b * cc[2 * j + 3]);
+                }
+                const uint4* u0 = reinterpret_cast<const uint4*>(h0);
+                const uint4* u1 = reinterpret_cast<const uint4*>(h1);
+                const int sw = (lane >> 1) & 3;
+                if constexpr (DH == 64) {
+                  const int pc = sub / 8;  // 16 columns = two 16-byte pieces
+#pragma unroll
+                  for (int q = 0; q < 2; ++q) {
+                    *reinterpret_cast<uint4*>(stg + lane * 64 + (((pc + q) ^ sw) << 4)) = u0[q];
+                    *reinterpret_cast<uint4*>(stg + kStageChunk + lane * 64 + (((pc + q) ^ sw) << 4)) = u1[q];
+                  }
+                } else {
+#pragma unroll
+                  for (int q = 0; q < 2; ++q) {
+                    *reinterpret_cast<uint4*>(stg + lane * 64 + ((q ^ sw) << 4)) = u0[q];
+                    *reinterpret_cast<uint4*>(stg + lane * 64 + (((2 + q) ^ sw) << 4)) = u1[q];
+                  }
+                }
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmap_out, stg, n, row0);
+                if constexpr (DH == 64) tma_store_2d(&tmap_out, stg + kStageChunk, n + 32, row0);
+                bulk_commit();
+              }
+            } else {
+              // V columns: acc + bias in fp16, 32 columns per staging block.
+#pragma unroll
+              for (int cc = 0; cc < DH; cc += 32) {
+                uint8_t* blk = stg + (cc / 32) * kStageChunk;
+                uint32_t r[16], r2[16];
+                tmem_ld16(t_row + c + cc, r);
+                tmem_ld16(t_row + c + cc + 16, r2);
+                tmem_ld_wait();
+                __half2 hv[16];
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                  hv[j / 2] = __floats2half2_rn(__uint_as_float(r[j]) + __ldg(p.bias + n + cc + j),
+                                                __uint_as_float(r[j + 1]) + __ldg(p.bias + n + cc + j + 1));
+                  hv[8 + j / 2] = __floats2half2_rn(__uint_as_float(r2[j]) + __ldg(p.bias + n + cc + 16 + j),
+                                                    __uint_as_float(r2[j + 1]) + __ldg(p.bias + n + cc + 17 + j));
+                }
+                stage_row64(blk, lane, reinterpret_cast<const uint4*>(hv));
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+#pragma unroll
+                for (int cc = 0; cc < DH; cc += 32) tma_store_2d(&tmap_out, stg + (cc / 32) * kStageChunk, n + cc, row0);
+                bulk_commit();
+              }
+            }
+          }
+        } else if constexpr (EPI == kEpiGeluF16) {
+#pragma unroll 1
+          for (int c = c_begin; c < c_end; c += 32) {
+            uint8_t* blk = stg + sbuf * kStageChunk;
+            float4 b[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) b[i] = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + c) + i);
+            uint32_t r[32];
+            tmem_ld16(t_row + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+            tmem_ld16(t_row + c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+            if (lane == 0) bulk_wait_read<1>();  // the store that last used this block has read it
+            tmem_ld_wait();
+            const float* bb = reinterpret_cast<const float*>(b);
+            __half2 hv[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2)
+              hv[j / 2] = __floats2half2_rn(gelu_fast(__uint_as_float(r[j]) + bb[j]),
+                                            gelu_fast(__uint_as_float(r[j + 1]) + bb[j + 1]));
+            __syncwarp();
+            stage_row64(blk, lane, reinterpret_cast<const uint4*>(hv));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_out, blk, n0 + c, row0);
+              bulk_commit();
+            }
+            sbuf ^= 1;
+          }
+        } else if constexpr (EPI == kEpiResidF32) {
+#pragma unroll 1
+          for (int c = c_begin; c < c_end; c += 16) {
+            uint8_t* blk = stg + sbuf * kStageChunk;
+            float4 b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              b[i] = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + n0 + c) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            uint32_t r[16];
+            tmem_ld16(t_row + c, r);
+            if (lane == 0) bulk_wait_read<1>();
+            tmem_ld_wait();
+            float4 v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              v[i] = make_float4(__uint_as_float(r[4 * i + 0]) + b[i].x, __uint_as_float(r[4 * i + 1]) + b[i].y,
+                                 __uint_as_float(r[4 * i + 2]) + b[i].z, __uint_as_float(r[4 * i + 3]) + b[i].w);
+            __syncwarp();
+            stage_row64(blk, lane, reinterpret_cast<const uint4*>(v));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_reduce_add_2d(&tmap_out, blk, n0 + c, row0);
+              bulk_commit();
+            }
+            sbuf ^= 1;
+          }
+        }
+      } else       if constexpr (EPI == kEpiQkvRope && (DH / 2) % 16 == 0) {
         // head_dim 32 / 64: rotate 16 (j, j + DH/2) pairs per step; the bias and cos/sin rows are
         // requested (float4) before the tensor-memory wait so their latency overlaps it.
         constexpr int HALF = DH / 2;
@@ -450,6 +623,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // Bulk stores still in flight complete before the CTA leaves.
+    if constexpr (TS) {
+      if (lane == 0) bulk_wait_all();
+    }
   }
 
   __syncthreads();
@@ -464,11 +641,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int EPI, int DH, int CG>
-cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms,
-                       cudaStream_t stream) {
-  using S = GemmShape<BN, CG>;
-  auto kern = gemm_tc_kernel<BN, EPI, DH, CG>;
+template <int BN, int EPI, int DH, int CG, bool TS>
+cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tout, const GemmParams& p,
+                       int num_sms, cudaStream_t stream) {
+  using S = GemmShape<BN, CG, TS>;
+  auto kern = gemm_tc_kernel<BN, EPI, DH, CG, TS>;
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
@@ -506,29 +683,42 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   const int clusters = tiles < max_clusters ? tiles : max_clusters;
   if (clusters <= 0) return cudaSuccess;
   cfg.gridDim = dim3(clusters * CG, 1, 1);
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, tout, p);
+}
+
+// Plain epilogues (no output tensor map) and the bulk-store ones where the output map is given,
+// the tile splits into whole 32-column blocks per epilogue warp, and the epilogue has a staged form.
+template <int BN, int EPI, int DH, int CG>
+cudaError_t launch_ts(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, const GemmParams& p,
+                      int num_sms, cudaStream_t s) {
+  constexpr bool kStaged = BN % 64 == 0 && (EPI == kEpiGeluF16 || EPI == kEpiResidF32 ||
+                                            (EPI == kEpiQkvRope && (DH == 64 || DH == 32)));
+  if constexpr (kStaged) {
+    if (tout != nullptr) return launch_one<BN, EPI, DH, CG, true>(ta, tb, *tout, p, num_sms, s);
+  }
+  return launch_one<BN, EPI, DH, CG, false>(ta, tb, tout ? *tout : ta, p, num_sms, s);
 }
 
 template <int BN, int CG>
-cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, int epi, int dh, const GemmParams& p,
-                         int num_sms, cudaStream_t s) {
+cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, int epi, int dh,
+                         const GemmParams& p, int num_sms, cudaStream_t s) {
   switch (epi) {
-    case kEpiGeluF16: return launch_one<BN, kEpiGeluF16, 0, CG>(ta, tb, p, num_sms, s);
-    case kEpiResidF32: return launch_one<BN, kEpiResidF32, 0, CG>(ta, tb, p, num_sms, s);
-    case kEpiGeluF32: return launch_one<BN, kEpiGeluF32, 0, CG>(ta, tb, p, num_sms, s);
-    case kEpiStoreF32: return launch_one<BN, kEpiStoreF32, 0, CG>(ta, tb, p, num_sms, s);
+    case kEpiGeluF16: return launch_ts<BN, kEpiGeluF16, 0, CG>(ta, tb, tout, p, num_sms, s);
+    case kEpiResidF32: return launch_ts<BN, kEpiResidF32, 0, CG>(ta, tb, tout, p, num_sms, s);
+    case kEpiGeluF32: return launch_one<BN, kEpiGeluF32, 0, CG, false>(ta, tb, ta, p, num_sms, s);
+    case kEpiStoreF32: return launch_one<BN, kEpiStoreF32, 0, CG, false>(ta, tb, ta, p, num_sms, s);
     case kEpiQkvRope:
       if constexpr (BN % 64 == 0) {
-        if (dh == 64) return launch_one<BN, kEpiQkvRope, 64, CG>(ta, tb, p, num_sms, s);
+        if (dh == 64) return launch_ts<BN, kEpiQkvRope, 64, CG>(ta, tb, tout, p, num_sms, s);
       }
       if constexpr (BN % 32 == 0) {
-        if (dh == 32) return launch_one<BN, kEpiQkvRope, 32, CG>(ta, tb, p, num_sms, s);
+        if (dh == 32) return launch_ts<BN, kEpiQkvRope, 32, CG>(ta, tb, tout, p, num_sms, s);
       }
       if constexpr (BN % 24 == 0) {
-        if (dh == 24) return launch_one<BN, kEpiQkvRope, 24, CG>(ta, tb, p, num_sms, s);
+        if (dh == 24) return launch_one<BN, kEpiQkvRope, 24, CG, false>(ta, tb, ta, p, num_sms, s);
       }
       if constexpr (BN % 16 == 0) {
-        if (dh == 16) return launch_one<BN, kEpiQkvRope, 16, CG>(ta, tb, p, num_sms, s);
+        if (dh == 16) return launch_one<BN, kEpiQkvRope, 16, CG, false>(ta, tb, ta, p, num_sms, s);
       }
       return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
@@ -536,10 +726,10 @@ cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, int epi, 
 }
 
 template <int BN>
-cudaError_t dispatch_cg(const CUtensorMap& ta, const CUtensorMap& tb, int epi, int dh, int cg, const GemmParams& p,
-                        int num_sms, cudaStream_t s) {
-  return cg == 2 ? dispatch_epi<BN, 2>(ta, tb, epi, dh, p, num_sms, s)
-                 : dispatch_epi<BN, 1>(ta, tb, epi, dh, p, num_sms, s);
+cudaError_t dispatch_cg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, int epi, int dh, int cg,
+                        const GemmParams& p, int num_sms, cudaStream_t s) {
+  return cg == 2 ? dispatch_epi<BN, 2>(ta, tb, tout, epi, dh, p, num_sms, s)
+                 : dispatch_epi<BN, 1>(ta, tb, tout, epi, dh, p, num_sms, s);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -576,6 +766,20 @@ bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr || (elem_bytes != 2 && elem_bytes != 4)) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * elem_bytes) & 15) || rows == 0) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * static_cast<uint64_t>(elem_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(64 / elem_bytes), 32};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int gemm_pick_bn(int N, int head_dim) {
   static const int kCandidates[] = {256, 240, 192, 160, 128};
   for (int bn : kCandidates) {
@@ -593,8 +797,8 @@ int gemm_pick_bn_any(int N) {
   return 0;
 }
 
-cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int head_dim, GemmParams p,
-                        int num_sms, cudaStream_t stream, int cta_pair) {
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, int bn, int epi,
+                        int head_dim, GemmParams p, int num_sms, cudaStream_t stream, int cta_pair) {
   if (p.M <= 0) return cudaSuccess;
   if (bn <= 0 || p.N % bn || p.K <= 0) return cudaErrorInvalidValue;
   // The CTA pair needs the wide tiles and at least two 128-row blocks of work.
@@ -602,22 +806,27 @@ cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, in
   p.num_m_blocks = (p.M + 128 * cg - 1) / (128 * cg);
   p.num_n_blocks = p.N / bn;
   switch (bn) {
-    case 256: return dispatch_cg<256>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
-    case 240: return dispatch_cg<240>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
-    case 192: return dispatch_cg<192>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
-    case 160: return dispatch_cg<160>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
-    case 128: return dispatch_cg<128>(ta, tb, epi, head_dim, cg, p, num_sms, stream);
+    case 256: return dispatch_cg<256>(ta, tb, tout, epi, head_dim, cg, p, num_sms, stream);
+    case 240: return dispatch_cg<240>(ta, tb, tout, epi, head_dim, cg, p, num_sms, stream);
+    case 192: return dispatch_cg<192>(ta, tb, tout, epi, head_dim, cg, p, num_sms, stream);
+    case 160: return dispatch_cg<160>(ta, tb, tout, epi, head_dim, cg, p, num_sms, stream);
+    case 128: return dispatch_cg<128>(ta, tb, tout, epi, head_dim, cg, p, num_sms, stream);
     // Narrow tiles serve the plain fp32-output GEMM only (odd output widths of esm_matmul_tiled).
     case 96:
-      return epi == kEpiStoreF32 ? launch_one<96, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+      return epi == kEpiStoreF32 ? launch_one<96, kEpiStoreF32, 0, 1, false>(ta, tb, ta, p, num_sms, stream)
+                               : cudaErrorInvalidValue;
     case 64:
-      return epi == kEpiStoreF32 ? launch_one<64, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+      return epi == kEpiStoreF32 ? launch_one<64, kEpiStoreF32, 0, 1, false>(ta, tb, ta, p, num_sms, stream)
+                               : cudaErrorInvalidValue;
     case 48:
-      return epi == kEpiStoreF32 ? launch_one<48, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+      return epi == kEpiStoreF32 ? launch_one<48, kEpiStoreF32, 0, 1, false>(ta, tb, ta, p, num_sms, stream)
+                               : cudaErrorInvalidValue;
     case 32:
-      return epi == kEpiStoreF32 ? launch_one<32, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+      return epi == kEpiStoreF32 ? launch_one<32, kEpiStoreF32, 0, 1, false>(ta, tb, ta, p, num_sms, stream)
+                               : cudaErrorInvalidValue;
     case 16:
-      return epi == kEpiStoreF32 ? launch_one<16, kEpiStoreF32, 0, 1>(ta, tb, p, num_sms, stream) : cudaErrorInvalidValue;
+      return epi == kEpiStoreF32 ? launch_one<16, kEpiStoreF32, 0, 1, false>(ta, tb, ta, p, num_sms, stream)
+                               : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }

@@ -33,6 +33,10 @@ struct GemmParams {
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                    uint32_t box_rows);
 
+// Tensor map for the epilogue's bulk stores: a row-major [rows, cols] matrix of fp16 (elem_bytes 2)
+// or fp32 (4), box = [32 rows, 64 bytes], 64-byte swizzle.
+bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld);
+
 // Largest supported tile width that divides N (and is a multiple of `head_dim` when non-zero).
 int gemm_pick_bn(int N, int head_dim);
 // Same, including the narrow widths (96..16) that only the kEpiStoreF32 epilogue supports.
@@ -41,7 +45,11 @@ int gemm_pick_bn_any(int N);
 // C[M, N] = A[M, K] . B[N, K]^T with the requested epilogue; A and B are fp16 K-major behind the
 // tensor maps (A box 128 rows, B box bn/2 rows). Persistent grid of at most num_sms CTAs; with
 // cta_pair != 0 (and bn >= 128, M > 128) tiles of 256 rows run on CTA pairs (tcgen05 cta_group::2).
-cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int epi, int head_dim,
-                        GemmParams p, int num_sms, cudaStream_t stream, int cta_pair);
+// `tout` (may be null) describes the output for the fp16 (kEpiQkvRope with head_dim 32 / 64,
+// kEpiGeluF16) and residual (kEpiResidF32) epilogues: with it those epilogues stage each
+// 32-row x 64-byte block in shared memory and write it with one bulk tensor store (or an L2
+// reduce-add for the residual), instead of per-thread stores to 32 different rows.
+cudaError_t gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, int bn, int epi,
+                        int head_dim, GemmParams p, int num_sms, cudaStream_t stream, int cta_pair);
 
 }  // namespace esm

@@ -125,7 +125,7 @@ extern "C" int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const v
   p.out = out;
   p.ldo = n_pad;
   p.err = slot->err;
-  e = esm::gemm_launch(ta, tb, bn, esm::kEpiStoreF32, 0, p, slot->num_sms, s, 1);
+  e = esm::gemm_launch(ta, tb, nullptr, bn, esm::kEpiStoreF32, 0, p, slot->num_sms, s, 1);
   if (e == cudaSuccess && padded_out)
     e = cudaMemcpy2DAsync(d_out, static_cast<size_t>(out_dim) * 4, out, static_cast<size_t>(n_pad) * 4,
                           static_cast<size_t>(out_dim) * 4, seq_len, cudaMemcpyDeviceToDevice, s);
