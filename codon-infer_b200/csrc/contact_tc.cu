@@ -240,15 +240,22 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
           acc[4 * g + u] = fmaf(w, pv, acc[4 * g + u]);
         }
       }
-      if (edge_key) {
-        // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i.
+      // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i. The lane
+      // that owns key 0 (or L-1) hands its 32 probabilities to the lanes of the warp, one query
+      // each, so the update is one coalesced reduction instead of 32 from a single thread.
+      unsigned edges = __ballot_sync(0xffffffffu, edge_key);
+      while (edges) {
+        const int src = __ffs(edges) - 1;
+        edges &= edges - 1;
+        float mine = 0.0f;
 #pragma unroll
         for (int u = 0; u < kQHalf; ++u) {
-          const int i = q0 + qh * kQHalf + u;
-          if (i < 1 || i > n) continue;
-          const float pv = fast_exp2(fmaf(__uint_as_float(s[u]), c, -lrow[u]));
-          atomicAdd(rh + (i - 1), (key == 0 ? 1.0f : 0.0f) - pv);
+          const float pu = __shfl_sync(0xffffffffu, fast_exp2(fmaf(__uint_as_float(s[u]), c, -lrow[u])), src);
+          if (lane == u) mine = pu;
         }
+        const int src_key = k0 + (warp & 3) * 32 + src;
+        const int i = q0 + qh * kQHalf + lane;
+        if (i >= 1 && i <= n) atomicAdd(rh + (i - 1), (src_key == 0 ? 1.0f : 0.0f) - mine);
       }
       if (inner_key) atomicAdd(rh + (key - 1), cs[0] + cs[1]);
     }
