@@ -1,4 +1,4 @@
-// Bidirectional attention on tcgen05 for head_dim 64, two query tiles per CTA. Same contract as
+// Bidirectional attention on tcgen05 for head_dim 64 and 32, two query tiles per CTA. Same contract as
 // attention_kernel in attention.cu (packed varlen sequences, keys past a sequence's end masked, O in
 // fp16, optional per-row log-sum-exp); replaces the reference attention loop (src/lib.rs:5206-5301).
 //
@@ -8,7 +8,8 @@
 //   warp 8      TMA producer: both Q tiles once, then 64-key K and V tiles into a 4-stage ring
 //   warp 9      tcgen05.mma issuer
 // The two query tiles share every K/V tile. Tensor memory (256 columns): S_t in [64 t, 64 t + 64),
-// O_t in [128 + 64 t, 192 + 64 t). The softmax writes P_t (fp16, two per column) over the first 32
+// O_t in [128 + DH t, 128 + DH (t + 1)). Head_dim 64 tiles use 128-byte rows with the 128-byte
+// swizzle, head_dim 32 tiles 64-byte rows with the 64-byte swizzle. The softmax writes P_t (fp16, two per column) over the first 32
 // columns of S_t and O_t += P_t V is issued with A read from tensor memory, so P never touches
 // shared memory. MMAs of one thread run in issue order, which orders every reuse of S_t:
 //   S0_0 S1_0 | PV0_0 S0_1 | PV1_0 S1_1 | PV0_1 S0_2 | ...
@@ -24,14 +25,21 @@ namespace {
 
 constexpr int kQ = 128;   // rows per query tile
 constexpr int kKV = 64;   // keys per K/V tile
-constexpr int kD = 64;    // head dim
 constexpr int kThreads2 = 320;
 constexpr int kStages2 = 4;
-constexpr int kQBytes = kQ * kD * 2;    // 16 KiB per query tile
-constexpr int kKVBytes = kKV * kD * 2;  // 8 KiB per K or V tile
-constexpr int kOffKV = 2 * kQBytes;
-constexpr int kOffBar = kOffKV + kStages2 * 2 * kKVBytes;
-constexpr int kSmem2 = kOffBar + 256 + 1024;
+
+// Tile geometry for head_dim DH (64: 128-byte rows, 128-byte swizzle; 32: 64-byte rows and swizzle).
+template <int DH>
+struct Tc2 {
+  static constexpr int kQBytes = kQ * DH * 2;    // one query tile
+  static constexpr int kKVBytes = kKV * DH * 2;  // one K or V tile
+  static constexpr int kOffKV = 2 * kQBytes;
+  static constexpr int kOffBar = kOffKV + kStages2 * 2 * kKVBytes;
+  static constexpr int kSmem = kOffBar + 256 + 1024;
+  static constexpr int kVStep = 16 * DH * 2;     // 16 keys of V
+  __device__ static uint64_t kdesc(uint32_t a) { return DH == 64 ? umma_sdesc_sw128(a) : umma_sdesc_sw64(a); }
+  __device__ static uint64_t vdesc(uint32_t a) { return DH == 64 ? umma_sdesc_sw128_mn(a) : umma_sdesc_sw64_mn(a); }
+};
 constexpr uint32_t kTmemCols2 = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 // The running max used for P is refreshed only when a row's max grows by more than 2^8 (in the
@@ -40,33 +48,38 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;
 
 // S_t = Q_t K_j^T into S_t's tensor-memory columns, then signal `bar`.
+template <int DH>
 __device__ __forceinline__ void issue_s(uint32_t tmem, uint32_t q_addr, uint32_t kv_addr, int t, int j, uint64_t* bar) {
+  using G = Tc2<DH>;
   constexpr uint32_t idesc_qk = umma_idesc_f16(kQ, kKV);
-  const uint32_t k_addr = kv_addr + (j % kStages2) * 2 * kKVBytes;
+  const uint32_t k_addr = kv_addr + (j % kStages2) * 2 * G::kKVBytes;
 #pragma unroll
-  for (int k = 0; k < kD / 16; ++k)
-    umma_f16(tmem + t * kKV, umma_sdesc_sw128(q_addr + t * kQBytes + k * 32), umma_sdesc_sw128(k_addr + k * 32),
-             idesc_qk, k > 0);
+  for (int k = 0; k < DH / 16; ++k)
+    umma_f16(tmem + t * kKV, G::kdesc(q_addr + t * G::kQBytes + k * 32), G::kdesc(k_addr + k * 32), idesc_qk, k > 0);
   umma_commit(bar);
 }
 
 // O_t += P_t V_j with P_t (64 keys = 32 columns of fp16 pairs) read from tensor memory.
+template <int DH>
 __device__ __forceinline__ void issue_pv(uint32_t tmem, uint32_t kv_addr, int t, int j, uint64_t* bar) {
-  constexpr uint32_t idesc_pv = umma_idesc_f16(kQ, kD) | (1u << 16);  // B (V) is MN-major
-  const uint32_t v_addr = kv_addr + (j % kStages2) * 2 * kKVBytes + kKVBytes;
+  using G = Tc2<DH>;
+  constexpr uint32_t idesc_pv = umma_idesc_f16(kQ, DH) | (1u << 16);  // B (V) is MN-major
+  const uint32_t v_addr = kv_addr + (j % kStages2) * 2 * G::kKVBytes + G::kKVBytes;
 #pragma unroll
   for (int k = 0; k < kKV / 16; ++k)
-    umma_f16_ts(tmem + 128 + t * kD, tmem + t * kKV + k * 8, umma_sdesc_sw128_mn(v_addr + k * 2048), idesc_pv,
+    umma_f16_ts(tmem + 128 + t * DH, tmem + t * kKV + k * 8, G::vdesc(v_addr + k * G::kVStep), idesc_pv,
                 (j > 0 || k > 0) ? 1u : 0u);
   umma_commit(bar);
 }
 
 // POLY of every 8 column pairs take their exponentials on the FP32 pipe (poly_exp2) instead of the
 // special-function unit, which is the bottleneck of the softmax at head_dim 64.
-template <int POLY>
+template <int DH, int POLY>
 __global__ void __launch_bounds__(kThreads2, 2)
     attention_tc2_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
                          const AttnParams p) {
+  using G = Tc2<DH>;
+  constexpr int kQBytes = G::kQBytes, kKVBytes = G::kKVBytes, kOffKV = G::kOffKV, kOffBar = G::kOffBar;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -117,8 +130,8 @@ __global__ void __launch_bounds__(kThreads2, 2)
       tma_prefetch_desc(&tmap_kv);
       const uint64_t pol = l2_policy_evict_normal();
       mbar_arrive_expect_tx(q_full, has1 ? 2 * kQBytes : kQBytes);
-      tma_load_2d(smem, &tmap_q, q_full, h * kD, start + q0, pol);
-      if (has1) tma_load_2d(smem + kQBytes, &tmap_q, q_full, h * kD, start + q0 + kQ, pol);
+      tma_load_2d(smem, &tmap_q, q_full, h * DH, start + q0, pol);
+      if (has1) tma_load_2d(smem + kQBytes, &tmap_q, q_full, h * DH, start + q0 + kQ, pol);
       bool ok = true;
       int j = 0;
       for (; j < nkv; ++j) {
@@ -129,8 +142,8 @@ __global__ void __launch_bounds__(kThreads2, 2)
         }
         uint8_t* dst = smem + kOffKV + st * 2 * kKVBytes;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
-        tma_load_2d(dst, &tmap_kv, &kv_full[st], p.d + h * kD, start + j * kKV, pol);
-        tma_load_2d(dst + kKVBytes, &tmap_kv, &kv_full[st], 2 * p.d + h * kD, start + j * kKV, pol);
+        tma_load_2d(dst, &tmap_kv, &kv_full[st], p.d + h * DH, start + j * kKV, pol);
+        tma_load_2d(dst + kKVBytes, &tmap_kv, &kv_full[st], 2 * p.d + h * DH, start + j * kKV, pol);
       }
       if (!ok) {  // let the copies in flight land before the CTA exits
         mbar_wait(q_full, 0, p.err, kDevTimeoutProducer);
@@ -146,15 +159,15 @@ __global__ void __launch_bounds__(kThreads2, 2)
       bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutMma);
       if (ok && mbar_wait(&kv_full[0], 0, p.err, kDevTimeoutMma)) {
         tc_fence_after();
-        issue_s(tmem, q_addr, kv_addr, 0, 0, &s_full[0]);
-        if (has1) issue_s(tmem, q_addr, kv_addr, 1, 0, &s_full[1]);
+        issue_s<DH>(tmem, q_addr, kv_addr, 0, 0, &s_full[0]);
+        if (has1) issue_s<DH>(tmem, q_addr, kv_addr, 1, 0, &s_full[1]);
       } else {
         ok = false;
       }
       for (int j = 0; j < nkv && ok; ++j) {
         if (!mbar_wait(&p_full[0], j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(tmem, kv_addr, 0, j, &o_full[0]);
+        issue_pv<DH>(tmem, kv_addr, 0, j, &o_full[0]);
         const bool next = j + 1 < nkv;
         if (next) {
           if (!mbar_wait(&kv_full[(j + 1) % kStages2], ((j + 1) / kStages2) & 1, p.err, kDevTimeoutMma)) {
@@ -162,15 +175,15 @@ __global__ void __launch_bounds__(kThreads2, 2)
             break;
           }
           tc_fence_after();
-          issue_s(tmem, q_addr, kv_addr, 0, j + 1, &s_full[0]);
+          issue_s<DH>(tmem, q_addr, kv_addr, 0, j + 1, &s_full[0]);
         }
         if (has1) {
           if (!mbar_wait(&p_full[1], j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(tmem, kv_addr, 1, j, &o_full[1]);
+          issue_pv<DH>(tmem, kv_addr, 1, j, &o_full[1]);
         }
         umma_commit(&kv_empty[j % kStages2]);
-        if (has1 && next) issue_s(tmem, q_addr, kv_addr, 1, j + 1, &s_full[1]);
+        if (has1 && next) issue_s<DH>(tmem, q_addr, kv_addr, 1, j + 1, &s_full[1]);
       }
       if (!ok) {
         umma_commit(drain);
@@ -185,7 +198,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
     if (t == 0 || has1) {
       const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
       const uint32_t t_s = tmem + lane_off + t * kKV;
-      const uint32_t t_o = tmem + lane_off + 128 + t * kD;
+      const uint32_t t_o = tmem + lane_off + 128 + t * DH;
       const float c = p.scale * kLog2e;
       float mc = -INFINITY;  // running max in the exp2 domain (max score * c)
       float l = 0.0f;
@@ -223,7 +236,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
           if (!mbar_wait(&o_full[t], (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
+          for (int hh = 0; hh < DH / 32; ++hh) {
             uint32_t o[32];
             tmem_ld32(t_o + hh * 32, o);
             tmem_ld_wait();
@@ -276,9 +289,9 @@ __global__ void __launch_bounds__(kThreads2, 2)
         tc_fence_after();
         const int row = q0 + t * kQ + r;
         const float inv = 1.0f / l;
-        __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * kD;
+        __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * DH;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < DH / 32; ++hh) {
           uint32_t o[32];
           tmem_ld32(t_o + hh * 32, o);
           tmem_ld_wait();
@@ -305,36 +318,43 @@ __global__ void __launch_bounds__(kThreads2, 2)
   }
 }
 
-}  // namespace
-
-template <int POLY>
+template <int DH, int POLY>
 cudaError_t launch_poly(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p, cudaStream_t s) {
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(configured & (1ull << dev))) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attention_tc2_kernel<POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
+    cudaError_t e = cudaFuncSetAttribute(attention_tc2_kernel<DH, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Tc2<DH>::kSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured |= (1ull << dev);
   }
   dim3 grid(p.n_work, p.H);
-  attention_tc2_kernel<POLY><<<grid, kThreads2, kSmem2, s>>>(tm_q, tm_kv, p);
+  attention_tc2_kernel<DH, POLY><<<grid, kThreads2, Tc2<DH>::kSmem, s>>>(tm_q, tm_kv, p);
   return cudaGetLastError();
 }
+
+template <int DH>
+cudaError_t launch_dh2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p, int poly_eighths,
+                       cudaStream_t s) {
+  switch (poly_eighths) {
+    case 0: return launch_poly<DH, 0>(tm_q, tm_kv, p, s);
+    case 1: return launch_poly<DH, 1>(tm_q, tm_kv, p, s);
+    case 2: return launch_poly<DH, 2>(tm_q, tm_kv, p, s);
+    case 3: return launch_poly<DH, 3>(tm_q, tm_kv, p, s);
+    case 4: return launch_poly<DH, 4>(tm_q, tm_kv, p, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
 
 cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
                                  int poly_eighths, cudaStream_t s) {
   if (p.n_work <= 0) return cudaSuccess;
-  if (p.dh != kD) return cudaErrorInvalidValue;
-  switch (poly_eighths) {
-    case 0: return launch_poly<0>(tm_q, tm_kv, p, s);
-    case 1: return launch_poly<1>(tm_q, tm_kv, p, s);
-    case 2: return launch_poly<2>(tm_q, tm_kv, p, s);
-    case 3: return launch_poly<3>(tm_q, tm_kv, p, s);
-    case 4: return launch_poly<4>(tm_q, tm_kv, p, s);
-    default: return cudaErrorInvalidValue;
-  }
+  if (p.dh == 64) return launch_dh2<64>(tm_q, tm_kv, p, poly_eighths, s);
+  if (p.dh == 32) return launch_dh2<32>(tm_q, tm_kv, p, poly_eighths, s);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace esm

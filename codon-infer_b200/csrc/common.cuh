@@ -166,6 +166,19 @@ __device__ __forceinline__ uint64_t umma_sdesc_sw128_mn(uint32_t saddr) {
   return d;
 }
 
+// The same two layouts with the 64-byte swizzle (rows of 64 bytes = 32 fp16; 8-row groups 512 bytes
+// apart), for head_dim 32 tiles. K sub-steps of 16 elements still advance the start by 32 bytes.
+__device__ __forceinline__ uint64_t umma_sdesc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(512 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(4) << 61;  // SWIZZLE_64B
+  return d;
+}
+__device__ __forceinline__ uint64_t umma_sdesc_sw64_mn(uint32_t saddr) { return umma_sdesc_sw64(saddr); }
+
 // Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |

@@ -766,6 +766,24 @@ bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_f16_box(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                       uint32_t box_rows, uint32_t box_cols, int swizzle_bytes) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr || (swizzle_bytes != 64 && swizzle_bytes != 128)) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15) || box_rows == 0 || box_rows > 256 ||
+      box_cols * 2 != static_cast<uint32_t>(swizzle_bytes))
+    return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr || (elem_bytes != 2 && elem_bytes != 4)) return false;

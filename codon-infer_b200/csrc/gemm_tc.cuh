@@ -33,6 +33,10 @@ struct GemmParams {
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                    uint32_t box_rows);
 
+// Same with an explicit box width (box_cols fp16 columns) and swizzle (64 or 128 bytes).
+bool make_tmap_f16_box(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                       uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
+
 // Tensor map for the epilogue's bulk stores: a row-major [rows, cols] matrix of fp16 (elem_bytes 2)
 // or fp32 (4), box = [32 rows, 64 bytes], 64-byte swizzle.
 bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld);

@@ -244,3 +244,16 @@ def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly):
     seqs = esm.random_sequences(len(lens), lens, seed=11)
     out = m.forward(seqs, want_hidden=True, want_contacts=True)
     compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
+
+
+def test_150m_shape_head_dim_32_attention(esm, orc):
+    # head_dim 32 (ESM-2 150M) on the two-tile tcgen05 attention (64-byte-swizzled tiles), with
+    # contacts reading its log-sum-exp, on lengths around the 64-key and 128/256-row tile edges.
+    base = esm.esm2_150m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    m, t, cw = build(esm, cfg, esm.DTYPE_FP32, seed=12)
+    lens = [5, 64, 65, 129, 256, 257, 302]
+    m.reserve(sum(lens), len(lens), 302, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=13)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_FP32, t, seqs, out, cw)
