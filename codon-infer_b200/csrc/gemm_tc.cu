@@ -799,7 +799,9 @@ bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t 
 }
 
 int gemm_pick_bn(int N, int head_dim) {
-  static const int kCandidates[] = {256, 240, 192, 160, 128};
+  // Widths that are multiples of 64 first: their epilogue warps split the tile into whole
+  // 32-column blocks, which the bulk-store epilogues need.
+  static const int kCandidates[] = {256, 192, 128, 240, 160};
   for (int bn : kCandidates) {
     if (N % bn) continue;
     if (head_dim > 0 && bn % head_dim) continue;

@@ -41,7 +41,8 @@ bool make_tmap_f16_box(CUtensorMap* map, const void* base, uint64_t rows, uint64
 // or fp32 (4), box = [32 rows, 64 bytes], 64-byte swizzle.
 bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld);
 
-// Largest supported tile width that divides N (and is a multiple of `head_dim` when non-zero).
+// Tile width that divides N (and is a multiple of `head_dim` when non-zero): the widest multiple of
+// 64 among 256/192/128 when one fits, else 240 or 160.
 int gemm_pick_bn(int N, int head_dim);
 // Same, including the narrow widths (96..16) that only the kEpiStoreF32 epilogue supports.
 int gemm_pick_bn_any(int N);
