@@ -125,19 +125,19 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
       constexpr uint32_t idesc_pv = umma_idesc_f16(kQ, kD) | (1u << 16);  // B (V) is MN-major
       const uint32_t q_addr = smem_u32(smem);
       const uint32_t p_addr = smem_u32(smem + kOffP);
-      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutMma);
+      bool ok = mbar_wait_spin(q_full, 0, p.err, kDevTimeoutMma);
       for (int j = 0; j < nkv && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_full[st], ph, p.err, kDevTimeoutMma)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait_spin(&kv_full[st], ph, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (j > 0 && !mbar_wait_spin(s_free, (j - 1) & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + kOffK + st * kKVBytes);
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k)
           umma_f16(t_s, umma_sdesc_sw128(q_addr + k * 32), umma_sdesc_sw128(k_addr + k * 32), idesc_qk, k > 0);
         umma_commit(s_full);
-        if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait_spin(p_full, j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + kOffV + st * kKVBytes);
 #pragma unroll
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
       }
       if (!ok) {
         umma_commit(drain);
-        mbar_wait(drain, 0, p.err, kDevTimeoutMma);
+        mbar_wait_spin(drain, 0, p.err, kDevTimeoutMma);
       }
     }
   } else {
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
     const int sw = r & 7;
     bool ok = true;
     for (int j = 0; j < nkv && ok; ++j) {
-      if (!mbar_wait(s_full, j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      if (!mbar_wait_spin(s_full, j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
       const int kvalid = len - j * kKV;  // keys of this tile inside the sequence (> 0)
       // Pass 1: row max (32 columns at a time keeps registers low). c > 0, so the max of the
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
         // Refresh the max of this warp's rows: O (after the previous P V) and l scale by alpha.
         const float m_new = fmaxf(mc, mx);
         const float alpha = fast_exp2(mc - m_new);
-        if (!mbar_wait(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+        if (!mbar_wait_spin(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
         mc = m_new;
       }
       // The previous P V must have consumed the P buffer before it is overwritten.
-      if (j > 0 && !mbar_wait(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+      if (j > 0 && !mbar_wait_spin(o_full, (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
       // Pass 2: P = exp2(S c - m) in fp16 into the 128-byte swizzled K-major tile (16-byte chunk k
       // of row r at chunk k ^ (r & 7)); keys past the sequence end get P = 0.
       float rsp[8];  // independent partial row sums
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kThreadsAt, 3)
         mbar_arrive(p_full);
       }
     }
-    if (ok && mbar_wait(o_full, (nkv - 1) & 1, p.err, kDevTimeoutEpilogue)) {
+    if (ok && mbar_wait_spin(o_full, (nkv - 1) & 1, p.err, kDevTimeoutEpilogue)) {
       tc_fence_after();
       const int row = q0 + r;
       const float inv = 1.0f / l;

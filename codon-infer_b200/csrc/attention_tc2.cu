@@ -156,8 +156,8 @@ __global__ void __launch_bounds__(kThreads2, 2)
     if (elect_one_sync()) {
       const uint32_t q_addr = smem_u32(smem);
       const uint32_t kv_addr = smem_u32(smem + kOffKV);
-      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutMma);
-      if (ok && mbar_wait(&kv_full[0], 0, p.err, kDevTimeoutMma)) {
+      bool ok = mbar_wait_spin(q_full, 0, p.err, kDevTimeoutMma);
+      if (ok && mbar_wait_spin(&kv_full[0], 0, p.err, kDevTimeoutMma)) {
         tc_fence_after();
         issue_s<DH>(tmem, q_addr, kv_addr, 0, 0, &s_full[0]);
         if (has1) issue_s<DH>(tmem, q_addr, kv_addr, 1, 0, &s_full[1]);
@@ -165,12 +165,12 @@ __global__ void __launch_bounds__(kThreads2, 2)
         ok = false;
       }
       for (int j = 0; j < nkv && ok; ++j) {
-        if (!mbar_wait(&p_full[0], j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait_spin(&p_full[0], j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
         issue_pv<DH>(tmem, kv_addr, 0, j, &o_full[0]);
         const bool next = j + 1 < nkv;
         if (next) {
-          if (!mbar_wait(&kv_full[(j + 1) % kStages2], ((j + 1) / kStages2) & 1, p.err, kDevTimeoutMma)) {
+          if (!mbar_wait_spin(&kv_full[(j + 1) % kStages2], ((j + 1) / kStages2) & 1, p.err, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
           issue_s<DH>(tmem, q_addr, kv_addr, 0, j + 1, &s_full[0]);
         }
         if (has1) {
-          if (!mbar_wait(&p_full[1], j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait_spin(&p_full[1], j & 1, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
           issue_pv<DH>(tmem, kv_addr, 1, j, &o_full[1]);
         }
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
       }
       if (!ok) {
         umma_commit(drain);
-        mbar_wait(drain, 0, p.err, kDevTimeoutMma);
+        mbar_wait_spin(drain, 0, p.err, kDevTimeoutMma);
       }
     }
   } else {
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
       float l = 0.0f;
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
-        if (!mbar_wait(&s_full[t], j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+        if (!mbar_wait_spin(&s_full[t], j & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
         tc_fence_after();
         const int kvalid = len - j * kKV;  // keys of this tile inside the sequence (> 0)
         // Pass 1: row max, 32 columns at a time (only the last tile needs the key mask).
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
           // Refresh the max of this warp's rows once the previous O += P V has landed.
           const float m_new = fmaxf(mc, mx);
           const float alpha = fast_exp2(mc - m_new);
-          if (!mbar_wait(&o_full[t], (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+          if (!mbar_wait_spin(&o_full[t], (j - 1) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int hh = 0; hh < DH / 32; ++hh) {
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(kThreads2, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
       }
-      if (ok && mbar_wait(&o_full[t], (nkv - 1) & 1, p.err, kDevTimeoutEpilogue)) {
+      if (ok && mbar_wait_spin(&o_full[t], (nkv - 1) & 1, p.err, kDevTimeoutEpilogue)) {
         tc_fence_after();
         const int row = q0 + t * kQ + r;
         const float inv = 1.0f / l;

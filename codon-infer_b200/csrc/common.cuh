@@ -60,35 +60,61 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// The waiting thread is suspended until the phase completes or kWaitSuspendNs pass, so spinning
-// producer / MMA threads do not take issue slots from the warps that do the math.
+// With kSleep the waiting thread is suspended until the phase completes or kWaitSuspendNs pass, so
+// spinning producer / MMA threads do not take issue slots from the warps that do the math. A thread
+// woken from that suspension resumes about a thousand cycles after the phase completes (measured in
+// the attention kernels), so waits on the critical path of a fine-grained handoff use kSleep =
+// false: try_wait then blocks only for the hardware's own short time limit.
 constexpr uint32_t kWaitSuspendNs = 1000000u;
+template <bool kSleep = true>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n"
-      ".reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-      "selp.u32 %0, 1, 0, p;\n"
-      "}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitSuspendNs)
-      : "memory");
+  if constexpr (kSleep) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitSuspendNs)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 // Bounded wait for phase `parity` of `bar`. Returns false (and records `code` in *err) once
 // `limit_ns` of %globaltimer have passed without the phase completing.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          uint64_t limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait(bar, parity)) return true;
+template <bool kSleep = true>
+__device__ __forceinline__ bool mbar_wait_t(uint64_t* bar, uint32_t parity, int* err, int code,
+                                            uint64_t limit_ns = kWaitLimitNs) {
+  if (mbar_try_wait<kSleep>(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kSleep>(bar, parity)) return true;
     if (globaltimer_ns() - t0 > limit_ns) {
       atomicOr(err, code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  return mbar_wait_t<true>(bar, parity, err, code, limit_ns);
+}
+// The same without the suspension (latency-critical handoffs).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+  return mbar_wait_t<false>(bar, parity, err, code, limit_ns);
 }
 
 // ---- TMA ----------------------------------------------------------------------------------------
@@ -262,6 +288,38 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Two 2^x of fp16 inputs in one special-function instruction (fp16 results).
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+// Packed FP32 pairs (sm_100): one instruction operates on both halves of a 64-bit register pair.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x on the FP32 pipe, to relieve the special-function unit where exp2 is the bottleneck. Range
 // reduction x = j + f with j = round(x) (add and subtract 1.5 * 2^23, which leaves j in the low
 // mantissa bits of the sum), f in [-0.5, 0.5]; 2^f by a degree-3 polynomial (coefficients: a
@@ -303,6 +361,45 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       "}\n" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Lean forms for an MMA issuer that shares its SM sub-partition with busy warps, where every
+// instruction it spends delays the next MMA: the 128-byte-swizzle descriptors (K-major and
+// MN-major alike: LBO 1, SBO 1024 bytes, version 1, SWIZZLE_128B) differ only in their low word,
+// the start address >> 4, so callers keep that word and add offsets to it (start addresses stay
+// below 256 KiB, the field's range); barriers are passed as shared-memory addresses.
+constexpr uint32_t kSw128DescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t umma_sw128_lo(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+__device__ __forceinline__ void umma_f16_lo(uint32_t tmem_d, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      ".reg .b64 ad, bd;\n"
+      "mov.b64 ad, {%1, %5};\n"
+      "mov.b64 bd, {%2, %5};\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ts_lo(uint32_t tmem_d, uint32_t tmem_a, uint32_t b_lo, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      ".reg .b64 bd;\n"
+      "mov.b64 bd, {%2, %5};\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_addr(uint32_t bar_saddr) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_saddr)
+               : "memory");
 }
 
 // ---- clusters and the CTA pair (cta_group::2) ----------------------------------------------------

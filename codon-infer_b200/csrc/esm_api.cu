@@ -29,12 +29,16 @@ struct esm_ctx {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   int cta_pair = 1;  // GEMM tiles on CTA pairs (cta_group::2); ESM_GEMM_CTA_PAIR=0 selects single CTAs
-  // Attention kernel for head_dim 64 (ESM_ATTN_TC): 2 = tcgen05, two query tiles per CTA with P in
-  // tensor memory (measured fastest); 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
-  int attn_tc = 2;
-  // Eighths of the softmax exponentials on the FP32 pipe (ESM_ATTN_POLY, 0..4); 0 by default, as
-  // moving them measured no faster: the special-function unit is not what bounds that kernel.
-  int attn_poly = 0;
+  // Attention kernel for head_dim 64 (ESM_ATTN_TC): 3 = tcgen05, two query tiles per CTA, 32-key
+  // tiles with two score buffers per tile (measured fastest); 2 = the same with 64-key tiles and one
+  // score buffer; 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
+  int attn_tc = 3;
+  // Eighths of the softmax exponentials on the FP32 pipe (ESM_ATTN_POLY, 0..4); -1 = the kernel's
+  // measured best (2 for kernel 3 with packed arithmetic, 0 otherwise).
+  int attn_poly = -1;
+  // Softmax arithmetic of kernel 3 (ESM_ATTN_EXP): 0 scalar FP32, 1 packed FP32 pairs (default,
+  // measured fastest), 2 fp16-pair exponentials.
+  int attn_exp = 1;
   int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
   std::string err;
@@ -96,6 +100,7 @@ struct esm_ctx {
   CUtensorMap tm_xn, tm_ao, tm_hb;
   CUtensorMap tm_qkv_q, tm_qkv_kv;  // qkv [T, 3d] with 64-column boxes of 128 / 64 rows
   CUtensorMap tm_qkv_q32, tm_qkv_kv32;  // the same with 32-column boxes (head_dim 32)
+  CUtensorMap tm_qkv_kv_r32;  // 64-column boxes of 32 rows (32-key K/V tiles)
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
@@ -394,7 +399,8 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
             esm::make_tmap_f16(&c->tm_qkv_q, c->qkv, rows, 3 * d, 3 * d, 128) &&
             esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64) &&
             esm::make_tmap_f16_box(&c->tm_qkv_q32, c->qkv, rows, 3 * d, 3 * d, 128, 32, 64) &&
-            esm::make_tmap_f16_box(&c->tm_qkv_kv32, c->qkv, rows, 3 * d, 3 * d, 64, 32, 64);
+            esm::make_tmap_f16_box(&c->tm_qkv_kv32, c->qkv, rows, 3 * d, 3 * d, 64, 32, 64) &&
+            esm::make_tmap_f16(&c->tm_qkv_kv_r32, c->qkv, rows, 3 * d, 3 * d, 32);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -585,7 +591,8 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
-  // head_dim 64 runs every tcgen05 kernel; head_dim 32 the two-tile one (for any ESM_ATTN_TC > 0).
+  // head_dim 64 runs every tcgen05 kernel; head_dim 32 the two-tile one with 64-key tiles (for any
+  // ESM_ATTN_TC > 0).
   const int attn_tc = dh == 64 ? c->attn_tc : (dh == 32 && c->attn_tc > 0 ? 2 : 0);
   const CUtensorMap& tm_att_q = dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q;
   const CUtensorMap& tm_att_kv = dh == 32 ? c->tm_qkv_kv32 : c->tm_qkv_kv;
@@ -624,8 +631,11 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
-      if (attn_tc == 2) {
-        ESM_CUDA(esm::launch_attention_tc2(tm_att_q, tm_att_kv, ap256, c->attn_poly, s));
+      if (attn_tc == 3) {
+        const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 ? 2 : 0);
+        ESM_CUDA(esm::launch_attention_tc3(c->tm_qkv_q, c->tm_qkv_kv_r32, ap256, poly, c->attn_exp, s));
+      } else if (attn_tc == 2) {
+        ESM_CUDA(esm::launch_attention_tc2(tm_att_q, tm_att_kv, ap256, std::max(0, c->attn_poly), s));
       } else if (attn_tc) {
         ESM_CUDA(esm::launch_attention_tc(c->tm_qkv_q, c->tm_qkv_kv, ap128, s));
       } else {
@@ -818,6 +828,7 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   if (const char* v = std::getenv("ESM_GEMM_CTA_PAIR")) c->cta_pair = std::atoi(v) != 0;
   if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v);
   if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(4, std::max(0, std::atoi(v)));
+  if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(2, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {

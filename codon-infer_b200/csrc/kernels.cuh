@@ -93,6 +93,10 @@ cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_k
 // query block); poly_eighths (0..4) of the softmax exponentials are computed on the FP32 pipe.
 cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
                                  int poly_eighths, cudaStream_t s);
+// Same with 32-key K/V tiles and two score buffers per query tile (attention_tc3.cu, head_dim 64):
+// tm_kv32 boxes are 32 rows x 64 columns.
+cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
+                                 int poly_eighths, int exp_mode, cudaStream_t s);
 
 // Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
 // recomputes P = softmax(q k^T * scale) tile by tile from the saved LSE, adds w * P into the

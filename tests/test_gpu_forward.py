@@ -228,18 +228,23 @@ def test_contact_kernels_agree(esm, monkeypatch):
     assert np.abs(maps[0] - maps[1]).max() <= 2e-4
 
 
-@pytest.mark.parametrize("attn,poly", [("1", "0"), ("2", "0"), ("2", "2"), ("2", "4")])
-def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly):
-    # Both tcgen05 attention kernels (ESM_ATTN_TC=1: one 128-row query tile per CTA; 2: two tiles
-    # per CTA sharing K/V, P in tensor memory, with ESM_ATTN_POLY eighths of the exponentials on
-    # the FP32 pipe) on lengths at and around the 64-key and 128/256-row tile edges, with contacts
-    # (which read the saved log-sum-exp).
+@pytest.mark.parametrize("attn,poly,exp", [("1", "0", "0"), ("2", "0", "0"), ("2", "2", "0"), ("2", "4", "0"),
+                                           ("3", "0", "0"), ("3", "2", "0"), ("3", "0", "1"), ("3", "2", "1"),
+                                           ("3", "0", "2")])
+def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly, exp):
+    # The tcgen05 attention kernels (ESM_ATTN_TC=1: one 128-row query tile per CTA; 2: two tiles
+    # per CTA sharing K/V, P in tensor memory; 3: the same with 32-key tiles and two score buffers
+    # per tile; ESM_ATTN_POLY eighths of the exponentials on the FP32 pipe; ESM_ATTN_EXP the softmax
+    # arithmetic of kernel 3: scalar, packed FP32 pairs, fp16-pair exponentials) on lengths at and
+    # around the 32/64-key and 128/256-row tile edges, with contacts (which read the saved
+    # log-sum-exp).
     monkeypatch.setenv("ESM_ATTN_TC", attn)
     monkeypatch.setenv("ESM_ATTN_POLY", poly)
+    monkeypatch.setenv("ESM_ATTN_EXP", exp)
     base = esm.esm2_650m()
     cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
     m, t, cw = build(esm, cfg, esm.DTYPE_Q4_0, seed=4)
-    lens = [7, 64, 65, 128, 129, 256, 257, 300, 513, 640]
+    lens = [7, 33, 64, 65, 97, 128, 129, 256, 257, 300, 513, 640]
     m.reserve(sum(lens), len(lens), 640, contacts=True)
     seqs = esm.random_sequences(len(lens), lens, seed=11)
     out = m.forward(seqs, want_hidden=True, want_contacts=True)
