@@ -234,13 +234,63 @@ struct LayerDst {
   int64_t blk_end[6];  // cumulative block counts
 };
 
-__global__ void dequant_layer_kernel(LayerSrc src, LayerDst dst, int64_t total_blocks) {
-  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < total_blocks;
-       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    int m = 0;
-    while (g >= dst.blk_end[m]) ++m;
-    const int64_t blk = g - (m == 0 ? 0 : dst.blk_end[m - 1]);
-    convert_block(src.dtype, src.w[m], blk, dst.dst[m]);
+// Elements [8 part, 8 part + 8) of a 32-element block, as load_block gives them. For BlockQ4_0,
+// elements 0..15 are the low nibbles of qs[0..15] and 16..31 the high nibbles, so part p reads the
+// eight bytes qs[8 (p & 1) .. 8 (p & 1) + 8).
+__device__ __forceinline__ void load_block_part(int dtype, const void* src, int64_t blk, int part, float (&v)[8]) {
+  if (dtype == 0) {
+    const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(src) + blk * 32 + part * 8);
+    const float4 a = s[0], c = s[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+  } else if (dtype == 1) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(src) + blk * kQ8BlockBytes);
+    const float ds = __uint_as_float(w[0]);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t q = w[1 + 2 * part + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[4 * i + j] = static_cast<float>(static_cast<int8_t>((q >> (8 * j)) & 0xFF)) * ds;
+    }
+  } else {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(src) + blk * kQ4BlockBytes);
+    const float ds = __uint_as_float(w[0]);
+    const int shift = part < 2 ? 0 : 4;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t q = w[1 + 2 * (part & 1) + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[4 * i + j] = static_cast<float>(static_cast<int>((q >> (8 * j + shift)) & 0x0F) - 8) * ds;
+    }
+  }
+}
+
+// A quarter block (8 elements) per thread, so each warp writes 512 contiguous bytes of fp16.
+__global__ void dequant_layer_kernel(LayerSrc src, LayerDst dst, int64_t total_quarters) {
+  for (int64_t g4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g4 < total_quarters;
+       g4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t g = g4 >> 2;
+    const int part = static_cast<int>(g4 & 3);
+    // Matrix of block g, selected with constant indices (no local-memory copy of the arrays).
+    const void* w = src.w[0];
+    __half* o = dst.dst[0];
+    int64_t base = 0;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      if (g >= dst.blk_end[i]) {
+        w = src.w[i + 1];
+        o = dst.dst[i + 1];
+        base = dst.blk_end[i];
+      }
+    }
+    const int64_t blk = g - base;
+    float v[8];
+    load_block_part(src.dtype, w, blk, part, v);
+    __half2 h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    *reinterpret_cast<uint4*>(o + blk * 32 + part * 8) = *reinterpret_cast<uint4*>(h);
   }
 }
 
@@ -318,6 +368,99 @@ __global__ void lm_decoder_kernel(const float* __restrict__ in, int T, int d, in
     }
     s = warp_sum(s);
     if (lane == 0) logits[static_cast<size_t>(row) * V + o] = s + (bias ? bias[o] : 0.0f);
+  }
+}
+
+// Token-tiled form of lm_decoder_kernel for V <= kDecGroups * kDecOut outputs. A CTA takes
+// kDecTok tokens: first their row statistics (one warp per row, as above), then the reduction over
+// d in chunks of kDecK: the chunk's normalised activations [kDecTok][kDecK] and decoder columns
+// [V][kDecK] are staged in shared memory, and thread (token t, group g) accumulates outputs
+// g, g + kDecGroups, ... of token t. Every decoder element read from shared memory is a broadcast
+// that serves a warp's 32 tokens.
+constexpr int kDecTok = 64, kDecK = 80, kDecGroups = 4, kDecOut = 10;
+constexpr int kDecLdX = kDecK + 4;  // padded row (conflict-free float4 reads across tokens)
+template <int NCH>
+__global__ void __launch_bounds__(256)
+    lm_decoder_tiled_kernel(const float* __restrict__ in, int T, int d, int do_ln, const float* __restrict__ ln_w,
+                            const float* __restrict__ ln_b, const float* __restrict__ W,
+                            const float* __restrict__ bias, int V, float* __restrict__ logits) {
+  __shared__ __align__(16) float xs[kDecTok * kDecLdX];
+  __shared__ __align__(16) float ws[kDecGroups * kDecOut * kDecK];
+  __shared__ float mean_s[kDecTok], inv_s[kDecTok];
+  const int t0 = blockIdx.x * kDecTok;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (do_ln) {
+    const int nchunks = (d / 4 - lane + 31) / 32;
+    for (int rr = warp; rr < kDecTok; rr += 8) {
+      const int row = t0 + rr;
+      float mean = 0.0f, inv = 0.0f;
+      if (row < T) {
+        float4 v[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          if (c >= nchunks) break;
+          v[c] = *reinterpret_cast<const float4*>(in + static_cast<size_t>(row) * d + 4 * (lane + 32 * c));
+        }
+        row_stats<NCH>(v, nchunks, d, mean, inv);
+      }
+      if (lane == 0) {
+        mean_s[rr] = mean;
+        inv_s[rr] = inv;
+      }
+    }
+  }
+  const int tok = threadIdx.x % kDecTok;
+  const int grp = threadIdx.x / kDecTok;
+  float acc[kDecOut];
+#pragma unroll
+  for (int i = 0; i < kDecOut; ++i) acc[i] = 0.0f;
+  for (int k0 = 0; k0 < d; k0 += kDecK) {
+    const int kc = min(kDecK, d - k0);  // multiple of 4
+    __syncthreads();  // row statistics written / previous chunk consumed
+    // Activations: kDecTok rows x kc columns, float4 per thread-step, normalised on the way in.
+    for (int e = threadIdx.x; e < kDecTok * (kc / 4); e += 256) {
+      const int r = e / (kc / 4), c4 = 4 * (e % (kc / 4));
+      const int row = t0 + r;
+      float4 x = row < T ? *reinterpret_cast<const float4*>(in + static_cast<size_t>(row) * d + k0 + c4)
+                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (do_ln) {
+        const float mu = mean_s[r], iv = inv_s[r];
+        const float4 ww = *reinterpret_cast<const float4*>(ln_w + k0 + c4);
+        const float4 bb = *reinterpret_cast<const float4*>(ln_b + k0 + c4);
+        x.x = ww.x * (x.x - mu) * iv + bb.x;
+        x.y = ww.y * (x.y - mu) * iv + bb.y;
+        x.z = ww.z * (x.z - mu) * iv + bb.z;
+        x.w = ww.w * (x.w - mu) * iv + bb.w;
+      }
+      *reinterpret_cast<float4*>(xs + r * kDecLdX + c4) = x;
+    }
+    // Decoder columns k0 .. k0 + kc of every output.
+    for (int e = threadIdx.x; e < V * (kc / 4); e += 256) {
+      const int o = e / (kc / 4), c4 = 4 * (e % (kc / 4));
+      *reinterpret_cast<float4*>(ws + o * kDecK + c4) =
+          __ldg(reinterpret_cast<const float4*>(W + static_cast<size_t>(o) * d + k0 + c4));
+    }
+    __syncthreads();
+    const float* xr = xs + tok * kDecLdX;
+    for (int k = 0; k < kc; k += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
+#pragma unroll
+      for (int i = 0; i < kDecOut; ++i) {
+        const int o = grp + kDecGroups * i;
+        if (o < V) {
+          const float4 w4 = *reinterpret_cast<const float4*>(ws + o * kDecK + k);
+          acc[i] += (xv.x * w4.x + xv.y * w4.y) + (xv.z * w4.z + xv.w * w4.w);
+        }
+      }
+    }
+  }
+  const int row = t0 + tok;
+  if (row < T) {
+#pragma unroll
+    for (int i = 0; i < kDecOut; ++i) {
+      const int o = grp + kDecGroups * i;
+      if (o < V) logits[static_cast<size_t>(row) * V + o] = acc[i] + (bias ? bias[o] : 0.0f);
+    }
   }
 }
 
@@ -421,9 +564,9 @@ cudaError_t launch_dequant_layer(const LayerSrc& src, __half* wqkv, __half* wo, 
     dst.blk_end[m] = acc;
   }
   const int threads = 256;
-  int64_t blocks = (acc + threads - 1) / threads;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  dequant_layer_kernel<<<static_cast<int>(blocks), threads, 0, s>>>(src, dst, acc);
+  int64_t blocks = (4 * acc + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  dequant_layer_kernel<<<static_cast<int>(blocks), threads, 0, s>>>(src, dst, 4 * acc);
   return cudaGetLastError();
 }
 
@@ -465,6 +608,14 @@ cudaError_t launch_lm_decoder(const float* in, int T, int d, int do_ln, const fl
                               const float* W, const float* bias, int V, float* logits, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (d % 4 || d > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
+  // Token-tiled kernel when the outputs fit its per-thread slots (ESM vocabularies: V = 33).
+  if (V <= kDecGroups * kDecOut) {
+    row_dispatch(d, [&](auto nch) {
+      lm_decoder_tiled_kernel<decltype(nch)::value><<<(T + kDecTok - 1) / kDecTok, 256, 0, s>>>(
+          in, T, d, do_ln, ln_w, ln_b, W, bias, V, logits);
+    });
+    return cudaGetLastError();
+  }
   row_dispatch(d, [&](auto nch) {
     lm_decoder_kernel<decltype(nch)::value><<<row_blocks(T), 32 * kRowWarps, 0, s>>>(in, T, d, do_ln, ln_w, ln_b, W,
                                                                                       bias, V, logits);
