@@ -4,23 +4,23 @@
 // in fp16, optional per-row log-sum-exp); replaces the reference attention loop
 // (src/lib.rs:5206-5301).
 //
-// One CTA per (sequence, 256-query block, head); 320 threads; two CTAs per SM.
+// One CTA per (sequence, 256-query block, head); 352 threads; two CTAs per SM.
 //   warps 0..3  softmax of query tile 0 (rows 0..127 of the block), one row per thread
 //   warps 4..7  softmax of query tile 1 (rows 128..255)
 //   warp 8      TMA producer: both Q tiles once, then 32-key K and V tiles into an 8-stage ring
-//   warp 9      tcgen05.mma issuer
+//   warp 9, 10  tcgen05.mma issuers of query tile 0 and 1
 // Tensor memory (256 columns): S_{t,b} (tile t, buffer b, 32 keys) in [32 (2t + b), +32), O_t in
 // [128 + 64 t, +64). Key tile j uses buffer j & 1. The softmax writes P (fp16 pairs) over the first
 // 16 columns of S_{t,b} and O_t += P V is issued with A read from tensor memory. Per tile the MMA
 // order is S(0) S(1) | PV(0) S(2) | PV(1) S(3) | ...: S(j + 2) overwrites the buffer PV(j) has
 // read, and MMAs of one thread execute in issue order.
 //
-// One barrier per score buffer, step[b], carries every MMA completion the softmax waits for: the
-// prologue commits S(b) to it, and MMA iteration j commits once, after PV_0(j) PV_1(j) S_0(j + 2)
-// S_1(j + 2), to step[j & 1]. Completion number n of step[b] (1-based) is therefore S(b + 2(n - 1))
-// and, for n >= 2, PV(b + 2(n - 2)). The softmax waits on each step[b] in order and never more than
-// one completion ahead of the last one it consumed on that barrier, so every parity wait is
-// unambiguous. (A single barrier per tile for the PVs would not be: at the end PV(n - 2) may still be
+// One barrier per (tile, score buffer), step[t][b], carries every MMA completion the tile's softmax
+// waits for: the tile's issuer commits S(b) to it in the prologue, and once per key tile j, after
+// PV(j) S(j + 2), to step[t][j & 1]. Completion number n of step[t][b] (1-based) is therefore
+// S(b + 2(n - 1)) and, for n >= 2, PV(b + 2(n - 2)). The softmax waits on each barrier in order and
+// never more than one completion ahead of the last one it consumed on that barrier, so every parity
+// wait is unambiguous. (A single barrier per tile for the PVs would not be: at the end PV(n - 2) may still be
 // outstanding, and a parity wait for PV(n - 1) would match the completed phase of PV(n - 3).)
 // O is rescaled in tensor memory only when a row max grows past the threshold, after PV(j - 1) has
 // completed. All waits are bounded.
@@ -34,7 +34,7 @@ namespace {
 constexpr int kQ = 128;   // rows per query tile
 constexpr int kKV = 32;   // keys per K/V tile
 constexpr int kD = 64;    // head dim
-constexpr int kThreads3 = 320;
+constexpr int kThreads3 = 352;
 constexpr int kStages3 = 8;
 constexpr int kQBytes = kQ * kD * 2;    // one query tile (16 KiB)
 constexpr int kKVBytes = kKV * kD * 2;  // one K or V tile (4 KiB)
@@ -64,10 +64,10 @@ __global__ void __launch_bounds__(kThreads3, 2)
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;               // [8]
   uint64_t* kv_empty = kv_full + kStages3;    // [8]
-  uint64_t* step = kv_empty + kStages3;       // [2 buffers]: S and PV completions (both tiles)
-  uint64_t* p_full = step + 2;                // [2 buffers]: P written (both tiles' softmax warps)
-  uint64_t* drain = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* step = kv_empty + kStages3;       // [2 tiles][2 buffers]: S and PV completions
+  uint64_t* p_full = step + 4;                // [2 tiles][2 buffers]: P written
+  uint64_t* drain = p_full + 4;               // [2 tiles]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int2 wk = p.work[blockIdx.x];
@@ -81,13 +81,13 @@ __global__ void __launch_bounds__(kThreads3, 2)
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages3; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], ntiles);  // one commit from each tile's MMA issuer
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&step[i], 1);
-      mbar_init(&p_full[i], 4 * ntiles);
+      mbar_init(&p_full[i], 4);
     }
-    mbar_init(drain, 1);
+    for (int t = 0; t < 2; ++t) mbar_init(&drain[t], 1);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -127,26 +127,30 @@ __global__ void __launch_bounds__(kThreads3, 2)
           mbar_wait(&kv_full[jj % kStages3], (jj / kStages3) & 1, p.err, kDevTimeoutProducer);
       }
     }
-  } else if (warp == 9) {
-    // ---------------- MMA issuer ----------------
-    // This warp shares its SM sub-partition with four busy softmax warps and gets a fraction of the
-    // issue slots, so the loop is kept to few instructions: descriptors are low words plus constant
-    // offsets, barriers are precomputed shared-memory addresses, and one p_full barrier per buffer
-    // collects both tiles' softmax warps (one wait per key tile instead of one per query tile).
-    if (elect_one_sync()) {
+  } else if (warp == 9 || warp == 10) {
+    // ---------------- MMA issuers: warp 9 for query tile 0, warp 10 for tile 1 ----------------
+    // An issuer shares its SM sub-partition with four busy softmax warps and gets a fraction of the
+    // issue slots, so each tile has its own (the two sit on different sub-partitions) and the loop
+    // is kept to few instructions: descriptors are low words plus constant offsets and barriers
+    // are precomputed shared-memory addresses. Each issuer's MMAs execute in its issue order, which
+    // is all the buffer reuse of its tile relies on; the K/V stages are released by one commit from
+    // each issuer (kv_empty counts ntiles arrivals).
+    const int t = warp - 9;
+    if (t < ntiles && elect_one_sync()) {
       constexpr uint32_t idesc_qk = umma_idesc_f16(kQ, kKV);
       constexpr uint32_t idesc_pv = umma_idesc_f16(kQ, kD) | (1u << 16);  // B (V) is MN-major
       constexpr uint32_t kStageLo = (2 * kKVBytes) >> 4, kVLo = kKVBytes >> 4, kQLo = kQBytes >> 4;
       constexpr uint32_t kVStepLo = (16 * kD * 2) >> 4;  // 16 keys of V
-      const uint32_t q_lo = umma_sw128_lo(smem_u32(smem));
+      const uint32_t q_lo = umma_sw128_lo(smem_u32(smem)) + t * kQLo;
       const uint32_t kv_lo = umma_sw128_lo(smem_u32(smem + kOffKV));
-      const uint32_t bar_step = smem_u32(step), bar_e = smem_u32(kv_empty);
+      const uint32_t bar_step = smem_u32(step + 2 * t), bar_e = smem_u32(kv_empty);
+      const uint32_t d_o = tmem + o_col(t);
       // S_{t, j&1} = Q_t K_j^T.
-      auto issue_s = [&](int t, int j) {
+      auto issue_s = [&](int j) {
         const uint32_t d = tmem + s_col(t, j & 1);
-        const uint32_t a = q_lo + t * kQLo, b = kv_lo + (j % kStages3) * kStageLo;
+        const uint32_t b = kv_lo + (j % kStages3) * kStageLo;
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k) umma_f16_lo(d, a + 2 * k, b + 2 * k, idesc_qk, k);
+        for (int k = 0; k < kD / 16; ++k) umma_f16_lo(d, q_lo + 2 * k, b + 2 * k, idesc_qk, k);
       };
       bool ok = mbar_wait_spin(q_full, 0, p.err, kDevTimeoutMma);
       for (int j = 0; j < 2 && j < nkv && ok; ++j) {
@@ -155,39 +159,35 @@ __global__ void __launch_bounds__(kThreads3, 2)
           break;
         }
         tc_fence_after();
-        for (int t = 0; t < ntiles; ++t) issue_s(t, j);
+        issue_s(j);
         umma_commit_addr(bar_step + 8 * j);
       }
       for (int j = 0; j < nkv && ok; ++j) {
         const int bj = j & 1;
-        const bool ahead = j + 2 < nkv;
-        if (!mbar_wait_spin(&p_full[bj], (j >> 1) & 1, p.err, kDevTimeoutMma)) {
+        if (!mbar_wait_spin(&p_full[2 * t + bj], (j >> 1) & 1, p.err, kDevTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        // O_t += P_t V_j with P (32 keys = 16 columns of fp16 pairs) read from buffer j & 1.
         const uint32_t v = kv_lo + (j % kStages3) * kStageLo + kVLo;
-        for (int t = 0; t < ntiles; ++t) {
-          // O_t += P_t V_j with P (32 keys = 16 columns of fp16 pairs) read from buffer j & 1.
 #pragma unroll
-          for (int k = 0; k < kKV / 16; ++k)
-            umma_f16_ts_lo(tmem + o_col(t), tmem + s_col(t, bj) + k * 8, v + k * kVStepLo, idesc_pv,
-                           (j > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kKV / 16; ++k)
+          umma_f16_ts_lo(d_o, tmem + s_col(t, bj) + k * 8, v + k * kVStepLo, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
         umma_commit_addr(bar_e + 8 * (j % kStages3));
-        if (ahead) {
+        if (j + 2 < nkv) {
           if (!mbar_wait_spin(&kv_full[(j + 2) % kStages3], ((j + 2) / kStages3) & 1, p.err, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          for (int t = 0; t < ntiles; ++t) issue_s(t, j + 2);
+          issue_s(j + 2);
         }
         umma_commit_addr(bar_step + 8 * bj);
       }
       if (!ok) {
-        umma_commit(drain);
-        mbar_wait_spin(drain, 0, p.err, kDevTimeoutMma);
+        umma_commit(&drain[t]);
+        mbar_wait_spin(&drain[t], 0, p.err, kDevTimeoutMma);
       }
     }
   } else {
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
         const int bj = j & 1;
-        if (!mbar_wait_spin(&step[bj], (j >> 1) & 1, p.err, kDevTimeoutEpilogue)) {
+        if (!mbar_wait_spin(&step[2 * t + bj], (j >> 1) & 1, p.err, kDevTimeoutEpilogue)) {
           ok = false;
           break;
         }
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
           const float alpha = fast_exp2(mc - m_new);
           // PV(j - 1) is completion number ((j - 1) >> 1) + 2 of step[(j - 1) & 1]: the phase with
           // 0-based index ((j - 1) >> 1) + 1.
-          if (!mbar_wait_spin(&step[(j - 1) & 1], (((j - 1) >> 1) + 1) & 1, p.err, kDevTimeoutEpilogue)) {
+          if (!mbar_wait_spin(&step[2 * t + ((j - 1) & 1)], (((j - 1) >> 1) + 1) & 1, p.err, kDevTimeoutEpilogue)) {
             ok = false;
             break;
           }
@@ -330,10 +330,10 @@ __global__ void __launch_bounds__(kThreads3, 2)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[bj]);
+        if (lane == 0) mbar_arrive(&p_full[2 * t + bj]);
       }
       const int jl = nkv - 1;
-      if (ok && mbar_wait_spin(&step[jl & 1], ((jl >> 1) + 1) & 1, p.err, kDevTimeoutEpilogue)) {
+      if (ok && mbar_wait_spin(&step[2 * t + (jl & 1)], ((jl >> 1) + 1) & 1, p.err, kDevTimeoutEpilogue)) {
         tc_fence_after();
         const int row = q0 + t * kQ + r;
         const float inv = 1.0f / l;
