@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
 #pragma unroll
     for (int k = 0; k < kIters; ++k) {
       const int idx = threadIdx.x + k * kThreadsCt;
-      if (idx < nh * kQry) lse_s[idx] = lv[k] * kLog2e;
+      if (idx < nh * kQry) lse_s[idx] = -lv[k] * kLog2e;  // stored negated: the exponent is S c + lse_s
     }
   }
   if (warp == 1) {
@@ -146,9 +146,10 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  float acc[kQHalf];  // M^T[key, q0 + 32 * qh + c] summed over heads (epilogue threads)
+  // M^T[key, q0 + 32 * qh + c] summed over heads (epilogue threads), as packed FP32 pairs (c, c + 1).
+  uint64_t acc2[kQHalf / 2];
 #pragma unroll
-  for (int c = 0; c < kQHalf; ++c) acc[c] = 0.0f;
+  for (int c = 0; c < kQHalf / 2; ++c) acc2[c] = 0ull;
   bool ok = true;
 
   if (warp == 0) {
@@ -226,19 +227,31 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
       const float w = wts[t];
       const float* lrow = lse_s + t * kQry + qh * kQHalf;
       float* rh = rbase + static_cast<size_t>(heads[t]) * n;
-      float cs[2] = {0.0f, 0.0f};
+      // Packed FP32 pairs (fma/add.f32x2) for the exponent, the column sum and M^T += w P.
+      const uint64_t w2 = f2_pack(w, w), c2 = f2_pack(c, c);
+      uint64_t cs2 = 0ull;
 #pragma unroll
       for (int g = 0; g < kQHalf / 4; ++g) {
         const float4 l4 = *reinterpret_cast<const float4*>(lrow + 4 * g);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float lu = u == 0 ? l4.x : u == 1 ? l4.y : u == 2 ? l4.z : l4.w;
-          // One exponential in four on the FP32 pipe, the rest on the special-function unit.
-          const float arg = fmaf(__uint_as_float(s[4 * g + u]), c, -lu);
-          const float pv = (u == 3) ? poly_exp2(arg) : fast_exp2(arg);
-          cs[u & 1] += pv;
-          acc[4 * g + u] = fmaf(w, pv, acc[4 * g + u]);
-        }
+        float a0, a1, a2, a3;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(s[4 * g]), __uint_as_float(s[4 * g + 1])), c2, f2_pack(l4.x, l4.y)),
+                  a0, a1);
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(s[4 * g + 2]), __uint_as_float(s[4 * g + 3])), c2,
+                         f2_pack(l4.z, l4.w)),
+                  a2, a3);
+        // One exponential in four on the FP32 pipe, the rest on the special-function unit.
+        const uint64_t p01 = f2_pack(fast_exp2(a0), fast_exp2(a1));
+        const uint64_t p23 = f2_pack(fast_exp2(a2), poly_exp2(a3));
+        cs2 = f2_add(cs2, f2_add(p01, p23));
+        acc2[2 * g] = f2_fma(w2, p01, acc2[2 * g]);
+        acc2[2 * g + 1] = f2_fma(w2, p23, acc2[2 * g + 1]);
+      }
+      float cs[2];
+      {
+        float x0, x1;
+        f2_unpack(cs2, x0, x1);
+        cs[0] = x0;
+        cs[1] = x1;
       }
       // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i. The lane
       // that owns key 0 (or L-1) hands its 32 probabilities to the lanes of the warp, one query
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
         float mine = 0.0f;
 #pragma unroll
         for (int u = 0; u < kQHalf; ++u) {
-          const float pu = __shfl_sync(0xffffffffu, fast_exp2(fmaf(__uint_as_float(s[u]), c, -lrow[u])), src);
+          const float pu = __shfl_sync(0xffffffffu, fast_exp2(fmaf(__uint_as_float(s[u]), c, lrow[u])), src);
           if (lane == u) mine = pu;
         }
         const int src_key = k0 + (warp & 3) * 32 + src;
@@ -267,7 +280,12 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
     const int kr = (warp & 3) * 32 + lane;
     const int qh = (warp - 2) >> 2;
 #pragma unroll
-    for (int cc = 0; cc < kQHalf; ++cc) stage[kr * kStageStride + qh * kQHalf + cc] = acc[cc];
+    for (int cc = 0; cc < kQHalf / 2; ++cc) {
+      float x0, x1;
+      f2_unpack(acc2[cc], x0, x1);
+      stage[kr * kStageStride + qh * kQHalf + 2 * cc] = x0;
+      stage[kr * kStageStride + qh * kQHalf + 2 * cc + 1] = x1;
+    }
   }
   __syncthreads();
   if (!failed && warp >= 2) {
