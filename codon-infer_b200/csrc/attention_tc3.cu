@@ -33,14 +33,19 @@ namespace {
 
 constexpr int kQ = 128;   // rows per query tile
 constexpr int kKV = 32;   // keys per K/V tile
-constexpr int kD = 64;    // head dim
 constexpr int kThreads3 = 352;
 constexpr int kStages3 = 8;
-constexpr int kQBytes = kQ * kD * 2;    // one query tile (16 KiB)
-constexpr int kKVBytes = kKV * kD * 2;  // one K or V tile (4 KiB)
-constexpr int kOffKV = 2 * kQBytes;
-constexpr int kOffBar = kOffKV + kStages3 * 2 * kKVBytes;
-constexpr int kSmem3 = kOffBar + 256 + 1024;
+// Tile geometry for head_dim DH: 64 (128-byte rows, 128-byte swizzle) or 32 (64-byte rows and
+// swizzle). The UMMA descriptors of both layouts differ only in the high word.
+template <int DH>
+struct Tc3 {
+  static constexpr int kQBytes = kQ * DH * 2;    // one query tile
+  static constexpr int kKVBytes = kKV * DH * 2;  // one K or V tile
+  static constexpr int kOffKV = 2 * kQBytes;
+  static constexpr int kOffBar = kOffKV + kStages3 * 2 * kKVBytes;
+  static constexpr int kSmem = kOffBar + 256 + 1024;
+  static constexpr uint32_t kDescHi = DH == 64 ? kSw128DescHi : kSw64DescHi;
+};
 constexpr uint32_t kTmemCols3 = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 // The running max used for P is refreshed only when a row's max grows by more than 2^8 (in the
@@ -49,18 +54,21 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;
 
 __device__ __forceinline__ uint32_t s_col(int t, int b) { return static_cast<uint32_t>(kKV * (2 * t + b)); }
-__device__ __forceinline__ uint32_t o_col(int t) { return static_cast<uint32_t>(128 + kD * t); }
+template <int DH>
+__device__ __forceinline__ uint32_t o_col(int t) { return static_cast<uint32_t>(128 + DH * t); }
 
 // POLY of every 8 column pairs take their exponentials on the FP32 pipe (poly_exp2) instead of the
 // special-function unit. EXP selects the softmax arithmetic: 0 scalar FP32, 1 packed FP32 pairs
 // (fma/add.f32x2) and three-input maxima, 2 the same with the exponentials taken on fp16 pairs.
-template <int POLY, int EXP>
+template <int DH, int POLY, int EXP>
 __global__ void __launch_bounds__(kThreads3, 2)
     attention_tc3_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
                          const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  using G = Tc3<DH>;
+  constexpr int kD = DH, kQBytes = G::kQBytes, kKVBytes = G::kKVBytes, kOffKV = G::kOffKV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;               // [8]
   uint64_t* kv_empty = kv_full + kStages3;    // [8]
@@ -144,13 +152,13 @@ __global__ void __launch_bounds__(kThreads3, 2)
       const uint32_t q_lo = umma_sw128_lo(smem_u32(smem)) + t * kQLo;
       const uint32_t kv_lo = umma_sw128_lo(smem_u32(smem + kOffKV));
       const uint32_t bar_step = smem_u32(step + 2 * t), bar_e = smem_u32(kv_empty);
-      const uint32_t d_o = tmem + o_col(t);
+      const uint32_t d_o = tmem + o_col<DH>(t);
       // S_{t, j&1} = Q_t K_j^T.
       auto issue_s = [&](int j) {
         const uint32_t d = tmem + s_col(t, j & 1);
         const uint32_t b = kv_lo + (j % kStages3) * kStageLo;
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k) umma_f16_lo(d, q_lo + 2 * k, b + 2 * k, idesc_qk, k);
+        for (int k = 0; k < kD / 16; ++k) umma_f16_lo<G::kDescHi>(d, q_lo + 2 * k, b + 2 * k, idesc_qk, k);
       };
       bool ok = mbar_wait_spin(q_full, 0, p.err, kDevTimeoutMma);
       for (int j = 0; j < 2 && j < nkv && ok; ++j) {
@@ -173,7 +181,8 @@ __global__ void __launch_bounds__(kThreads3, 2)
         const uint32_t v = kv_lo + (j % kStages3) * kStageLo + kVLo;
 #pragma unroll
         for (int k = 0; k < kKV / 16; ++k)
-          umma_f16_ts_lo(d_o, tmem + s_col(t, bj) + k * 8, v + k * kVStepLo, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts_lo<G::kDescHi>(d_o, tmem + s_col(t, bj) + k * 8, v + k * kVStepLo, idesc_pv,
+                                     (j > 0 || k > 0) ? 1u : 0u);
         umma_commit_addr(bar_e + 8 * (j % kStages3));
         if (j + 2 < nkv) {
           if (!mbar_wait_spin(&kv_full[(j + 2) % kStages3], ((j + 2) / kStages3) & 1, p.err, kDevTimeoutMma)) {
@@ -197,7 +206,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
     const int r = quarter * 32 + lane;  // row inside the tile = TMEM lane
     if (t < ntiles) {
       const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-      const uint32_t t_o = tmem + lane_off + o_col(t);
+      const uint32_t t_o = tmem + lane_off + o_col<DH>(t);
       const float c = p.scale * kLog2e;
       float mc = -INFINITY;  // running max in the exp2 domain (max score * c)
       float l = 0.0f;
@@ -366,19 +375,19 @@ __global__ void __launch_bounds__(kThreads3, 2)
   }
 }
 
-template <int POLY, int EXP>
+template <int DH, int POLY, int EXP>
 cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p, cudaStream_t s) {
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(configured & (1ull << dev))) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attention_tc3_kernel<POLY, EXP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3);
+    cudaError_t e = cudaFuncSetAttribute(attention_tc3_kernel<DH, POLY, EXP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Tc3<DH>::kSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured |= (1ull << dev);
   }
   dim3 grid(p.n_work, p.H);
-  attention_tc3_kernel<POLY, EXP><<<grid, kThreads3, kSmem3, s>>>(tm_q, tm_kv32, p);
+  attention_tc3_kernel<DH, POLY, EXP><<<grid, kThreads3, Tc3<DH>::kSmem, s>>>(tm_q, tm_kv32, p);
   return cudaGetLastError();
 }
 
@@ -387,20 +396,25 @@ cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, co
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s) {
   if (p.n_work <= 0) return cudaSuccess;
-  if (p.dh != kD) return cudaErrorInvalidValue;
-  if (exp_mode == 2) return launch_poly3<0, 2>(tm_q, tm_kv32, p, s);
+  if (p.dh == 32) {  // the default arithmetic, and scalar FP32 for comparison
+    if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1>(tm_q, tm_kv32, p, s)
+                                                : launch_poly3<32, 2, 1>(tm_q, tm_kv32, p, s);
+    return launch_poly3<32, 0, 0>(tm_q, tm_kv32, p, s);
+  }
+  if (p.dh != 64) return cudaErrorInvalidValue;
+  if (exp_mode == 2) return launch_poly3<64, 0, 2>(tm_q, tm_kv32, p, s);
   if (exp_mode == 1) {
     switch (poly_eighths) {
-      case 0: return launch_poly3<0, 1>(tm_q, tm_kv32, p, s);
-      case 1: return launch_poly3<1, 1>(tm_q, tm_kv32, p, s);
-      case 2: return launch_poly3<2, 1>(tm_q, tm_kv32, p, s);
-      default: return launch_poly3<3, 1>(tm_q, tm_kv32, p, s);
+      case 0: return launch_poly3<64, 0, 1>(tm_q, tm_kv32, p, s);
+      case 1: return launch_poly3<64, 1, 1>(tm_q, tm_kv32, p, s);
+      case 2: return launch_poly3<64, 2, 1>(tm_q, tm_kv32, p, s);
+      default: return launch_poly3<64, 3, 1>(tm_q, tm_kv32, p, s);
     }
   }
   switch (poly_eighths) {
-    case 0: return launch_poly3<0, 0>(tm_q, tm_kv32, p, s);
-    case 1: return launch_poly3<1, 0>(tm_q, tm_kv32, p, s);
-    default: return launch_poly3<2, 0>(tm_q, tm_kv32, p, s);
+    case 0: return launch_poly3<64, 0, 0>(tm_q, tm_kv32, p, s);
+    case 1: return launch_poly3<64, 1, 0>(tm_q, tm_kv32, p, s);
+    default: return launch_poly3<64, 2, 0>(tm_q, tm_kv32, p, s);
   }
 }
 

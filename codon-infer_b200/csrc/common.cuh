@@ -369,7 +369,10 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
 // the start address >> 4, so callers keep that word and add offsets to it (start addresses stay
 // below 256 KiB, the field's range); barriers are passed as shared-memory addresses.
 constexpr uint32_t kSw128DescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+// The 64-byte-swizzle layouts (SBO 512 bytes, layout type 4) share the same low-word form.
+constexpr uint32_t kSw64DescHi = (512u >> 4) | (1u << 14) | (4u << 29);
 __device__ __forceinline__ uint32_t umma_sw128_lo(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+template <uint32_t HI = kSw128DescHi>
 __device__ __forceinline__ void umma_f16_lo(uint32_t tmem_d, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
@@ -381,9 +384,10 @@ __device__ __forceinline__ void umma_f16_lo(uint32_t tmem_d, uint32_t a_lo, uint
       "setp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, p;\n"
       "}\n" ::"r"(tmem_d),
-      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(HI)
       : "memory");
 }
+template <uint32_t HI = kSw128DescHi>
 __device__ __forceinline__ void umma_f16_ts_lo(uint32_t tmem_d, uint32_t tmem_a, uint32_t b_lo, uint32_t idesc,
                                                uint32_t accumulate) {
   asm volatile(
@@ -394,7 +398,7 @@ __device__ __forceinline__ void umma_f16_ts_lo(uint32_t tmem_d, uint32_t tmem_a,
       "setp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %3, p;\n"
       "}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
+      "r"(tmem_a), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(HI)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit_addr(uint32_t bar_saddr) {

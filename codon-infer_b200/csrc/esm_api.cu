@@ -100,7 +100,8 @@ struct esm_ctx {
   CUtensorMap tm_xn, tm_ao, tm_hb;
   CUtensorMap tm_qkv_q, tm_qkv_kv;  // qkv [T, 3d] with 64-column boxes of 128 / 64 rows
   CUtensorMap tm_qkv_q32, tm_qkv_kv32;  // the same with 32-column boxes (head_dim 32)
-  CUtensorMap tm_qkv_kv_r32;  // 64-column boxes of 32 rows (32-key K/V tiles)
+  CUtensorMap tm_qkv_kv_r32;    // 64-column boxes of 32 rows (32-key K/V tiles, head_dim 64)
+  CUtensorMap tm_qkv_kv32_r32;  // 32-column boxes of 32 rows, 64-byte swizzle (head_dim 32)
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
@@ -400,7 +401,8 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
             esm::make_tmap_f16(&c->tm_qkv_kv, c->qkv, rows, 3 * d, 3 * d, 64) &&
             esm::make_tmap_f16_box(&c->tm_qkv_q32, c->qkv, rows, 3 * d, 3 * d, 128, 32, 64) &&
             esm::make_tmap_f16_box(&c->tm_qkv_kv32, c->qkv, rows, 3 * d, 3 * d, 64, 32, 64) &&
-            esm::make_tmap_f16(&c->tm_qkv_kv_r32, c->qkv, rows, 3 * d, 3 * d, 32);
+            esm::make_tmap_f16(&c->tm_qkv_kv_r32, c->qkv, rows, 3 * d, 3 * d, 32) &&
+            esm::make_tmap_f16_box(&c->tm_qkv_kv32_r32, c->qkv, rows, 3 * d, 3 * d, 32, 32, 64);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -591,9 +593,9 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
-  // head_dim 64 runs every tcgen05 kernel; head_dim 32 the two-tile one with 64-key tiles (for any
-  // ESM_ATTN_TC > 0).
-  const int attn_tc = dh == 64 ? c->attn_tc : (dh == 32 && c->attn_tc > 0 ? 2 : 0);
+  // head_dim 64 runs every tcgen05 kernel; head_dim 32 the two-tile ones (3: double-buffered,
+  // the default; any other ESM_ATTN_TC > 0: 64-key tiles).
+  const int attn_tc = dh == 64 ? c->attn_tc : (dh == 32 && c->attn_tc > 0 ? (c->attn_tc == 3 ? 3 : 2) : 0);
   const CUtensorMap& tm_att_q = dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q;
   const CUtensorMap& tm_att_kv = dh == 32 ? c->tm_qkv_kv32 : c->tm_qkv_kv;
   esm::AttnParams ap128 = ap;
@@ -633,7 +635,9 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
       if (attn_tc == 3) {
         const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 ? 2 : 0);
-        ESM_CUDA(esm::launch_attention_tc3(c->tm_qkv_q, c->tm_qkv_kv_r32, ap256, poly, c->attn_exp, s));
+        ESM_CUDA(esm::launch_attention_tc3(dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q,
+                                           dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32, ap256, poly, c->attn_exp,
+                                           s));
       } else if (attn_tc == 2) {
         ESM_CUDA(esm::launch_attention_tc2(tm_att_q, tm_att_kv, ap256, std::max(0, c->attn_poly), s));
       } else if (attn_tc) {

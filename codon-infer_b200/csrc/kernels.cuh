@@ -93,8 +93,8 @@ cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_k
 // query block); poly_eighths (0..4) of the softmax exponentials are computed on the FP32 pipe.
 cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
                                  int poly_eighths, cudaStream_t s);
-// Same with 32-key K/V tiles and two score buffers per query tile (attention_tc3.cu, head_dim 64):
-// tm_kv32 boxes are 32 rows x 64 columns.
+// Same with 32-key K/V tiles and two score buffers per query tile (attention_tc3.cu, head_dim 64 or
+// 32): tm_kv32 boxes are 32 rows x head_dim columns (128- or 64-byte swizzle, as tm_q).
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s);
 

@@ -251,13 +251,16 @@ def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly, exp):
     compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
 
 
-def test_150m_shape_head_dim_32_attention(esm, orc):
-    # head_dim 32 (ESM-2 150M) on the two-tile tcgen05 attention (64-byte-swizzled tiles), with
-    # contacts reading its log-sum-exp, on lengths around the 64-key and 128/256-row tile edges.
+@pytest.mark.parametrize("attn", ["3", "2"])
+def test_150m_shape_head_dim_32_attention(esm, orc, monkeypatch, attn):
+    # head_dim 32 (ESM-2 150M) on the two-tile tcgen05 attention kernels (64-byte-swizzled tiles;
+    # 3: 32-key tiles with two score buffers per tile, the default; 2: 64-key tiles), with contacts
+    # reading the log-sum-exp, on lengths around the 32/64-key and 128/256-row tile edges.
+    monkeypatch.setenv("ESM_ATTN_TC", attn)
     base = esm.esm2_150m()
     cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
     m, t, cw = build(esm, cfg, esm.DTYPE_FP32, seed=12)
-    lens = [5, 64, 65, 129, 256, 257, 302]
+    lens = [5, 33, 64, 65, 129, 256, 257, 302]
     m.reserve(sum(lens), len(lens), 302, contacts=True)
     seqs = esm.random_sequences(len(lens), lens, seed=13)
     out = m.forward(seqs, want_hidden=True, want_contacts=True)
