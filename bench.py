@@ -274,10 +274,15 @@ def run_ours(args):
     host_tok = torch.from_numpy(host_tokens).pin_memory()
     host_logits = torch.empty(batch, Lmax, cfg.vocab_size, dtype=torch.float32).pin_memory()
     tok_np, log_np = host_tok.numpy(), host_logits.numpy()
+    host_con, con_np = None, None
+    if c["contacts"]:
+        np_ = max(Lmax - 2, 0)
+        host_con = torch.empty(batch, np_, np_, dtype=torch.float32).pin_memory()
+        con_np = host_con.numpy()
     d2h = batch * Lmax * cfg.vocab_size * 4 + (batch * max(Lmax - 2, 0) ** 2 * 4 if c["contacts"] else 0)
 
     def e2e_step():
-        model.forward(tok_np, lengths=lengths, logits_out=log_np, want_contacts=c["contacts"])
+        model.forward(tok_np, lengths=lengths, logits_out=log_np, want_contacts=c["contacts"], contacts_out=con_np)
 
     e2e_steps = max(1, min(args.steps, 5))
     e2e_step()

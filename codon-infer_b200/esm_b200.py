@@ -307,12 +307,16 @@ class Model:
         self._chk(lib().esm_reserve(self._ctx, max_tokens, max_seqs, max_len, int(contacts)), "esm_reserve")
 
     def forward(self, seqs, lengths=None, want_hidden: bool = False, want_contacts: bool = False,
-                logits_out: np.ndarray | None = None) -> dict:
+                logits_out: np.ndarray | None = None, hidden_out: np.ndarray | None = None,
+                contacts_out: np.ndarray | None = None) -> dict:
         """Batched forward_bidirectional from host memory.
 
         `seqs` is a list of int token arrays, or a right-padded int32 [B, Lmax] array together with
-        `lengths`. `logits_out` may be a preallocated (e.g. pinned) float32 [B, Lmax, vocab] array.
-        Returns padded outputs; padding positions are zero."""
+        `lengths`. `logits_out`, `hidden_out` and `contacts_out` may be preallocated (e.g. pinned)
+        float32 arrays of shape [B, Lmax, vocab], [B, Lmax, dim] and [B, Lmax - 2, Lmax - 2]; a
+        contact map of a long batch is large (536 MB for 8 x 4096), and copying it into fresh
+        pageable memory on every call costs more than the forward. Returns padded outputs; padding
+        positions are zero."""
         if isinstance(seqs, np.ndarray) and seqs.ndim == 2:
             tokens = np.ascontiguousarray(seqs, dtype=np.int32)
             lengths = np.ascontiguousarray(lengths, dtype=np.int32)
@@ -327,8 +331,15 @@ class Model:
             logits_out = np.empty((B, Lmax, cfg.vocab_size), dtype=np.float32)
         assert logits_out.shape == (B, Lmax, cfg.vocab_size) and logits_out.dtype == np.float32
         assert logits_out.flags.c_contiguous
-        hidden = np.empty((B, Lmax, cfg.dim), dtype=np.float32) if want_hidden else None
-        contacts = np.empty((B, max(Lmax - 2, 0), max(Lmax - 2, 0)), dtype=np.float32) if want_contacts else None
+        hidden = None
+        if want_hidden:
+            hidden = hidden_out if hidden_out is not None else np.empty((B, Lmax, cfg.dim), dtype=np.float32)
+            assert hidden.shape == (B, Lmax, cfg.dim) and hidden.dtype == np.float32 and hidden.flags.c_contiguous
+        contacts = None
+        if want_contacts:
+            np_ = max(Lmax - 2, 0)
+            contacts = contacts_out if contacts_out is not None else np.empty((B, np_, np_), dtype=np.float32)
+            assert contacts.shape == (B, np_, np_) and contacts.dtype == np.float32 and contacts.flags.c_contiguous
         self._chk(lib().esm_forward(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits_out), _p(hidden),
                                     _p(contacts)), "esm_forward")
         res = {"logits": logits_out, "lengths": lengths}

@@ -251,6 +251,28 @@ def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly, exp):
     compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
 
 
+def test_preallocated_outputs(esm):
+    # Caller-owned output arrays (the pinned buffers a serving loop reuses) receive exactly what
+    # the allocating call returns.
+    cfg = esm.esm2_8m()
+    m, _, _ = build(esm, cfg, esm.DTYPE_FP32)
+    lens = [40, 67]
+    m.reserve(sum(lens), len(lens), 67, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=21)
+    ref = m.forward(seqs, want_hidden=True, want_contacts=True)
+    B, L = len(lens), max(lens)
+    lo = np.full((B, L, cfg.vocab_size), np.nan, dtype=np.float32)
+    ho = np.full((B, L, cfg.dim), np.nan, dtype=np.float32)
+    co = np.full((B, L - 2, L - 2), np.nan, dtype=np.float32)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True, logits_out=lo, hidden_out=ho, contacts_out=co)
+    assert out["logits"] is lo and out["hidden"] is ho and out["contacts"] is co
+    np.testing.assert_array_equal(lo, ref["logits"])
+    np.testing.assert_array_equal(ho, ref["hidden"])
+    # The APC row sums are accumulated with atomics, so contacts may differ in the last bits.
+    np.testing.assert_allclose(co, ref["contacts"], rtol=0, atol=1e-6)
+    m.close()
+
+
 @pytest.mark.parametrize("attn", ["3", "2"])
 def test_150m_shape_head_dim_32_attention(esm, orc, monkeypatch, attn):
     # head_dim 32 (ESM-2 150M) on the two-tile tcgen05 attention kernels (64-byte-swizzled tiles;
