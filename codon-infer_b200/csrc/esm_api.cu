@@ -224,18 +224,32 @@ int build_weight_maps(esm_ctx* c) {
   return ok ? ESM_OK : fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for a weight matrix");
 }
 
-int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* const* tensors, const size_t* sizes) {
+// Tensors of a Q8_0 / Q4_0 model that are stored as blocks (EsmWeights::quantize_q8 / quantize_q4,
+// src/lib.rs:559-607): the six matrices of every layer, and for Q8_0 the token embedding.
+uint32_t quantized_tensors(int dtype) {
+  const uint32_t mats = (1u << 3) | (1u << 5) | (1u << 7) | (1u << 9) | (1u << 13) | (1u << 15);
+  return dtype == ESM_DTYPE_Q8_0 ? (mats | 1u) : (dtype == ESM_DTYPE_Q4_0 ? mats : 0u);
+}
+
+// Uploads a weight set. Tensor i with bit i of `quantize_mask` set is given as FP32 host data
+// (sizes[i] = its FP32 byte size) and is quantized to `dtype` blocks on the device, straight into
+// its device allocation; every other tensor is given in its `dtype` layout.
+int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* const* tensors, const size_t* sizes,
+                   uint32_t quantize_mask = 0) {
   std::string why;
   if (dtype < 0 || dtype > 2) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0 or Q4_0");
   if (!shape_supported(cfg, &why)) return fail(c, ESM_EINVAL, "unsupported model shape: " + why);
   int64_t expect[ESM_NUM_TENSORS];
   esm::tensor_layout(cfg, dtype, expect);
+  const int64_t block_bytes = dtype == ESM_DTYPE_Q8_0 ? 36 : 20;
   for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
     if (tensors[i] == nullptr && !(i == 19 && sizes[i] == 0))
       return fail(c, ESM_EINVAL, "tensor " + std::to_string(i) + " is null");
-    if (i < 19 && static_cast<int64_t>(sizes[i]) != expect[i])
+    const bool q = (quantize_mask >> i) & 1u;
+    const int64_t want = q ? expect[i] / block_bytes * 128 : expect[i];  // 32 floats per block
+    if (i < 19 && static_cast<int64_t>(sizes[i]) != want)
       return fail(c, ESM_EFORMAT, "tensor " + std::to_string(i) + " has " + std::to_string(sizes[i]) +
-                                      " bytes, expected " + std::to_string(expect[i]));
+                                      " bytes, expected " + std::to_string(want));
   }
   if (sizes[19] % 4) return fail(c, ESM_EFORMAT, "classifier byte size is not a multiple of 4");
 
@@ -258,10 +272,27 @@ int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* con
   const int64_t d = cfg.dim, F = cfg.hidden_dim, nl = cfg.n_layers, V = cfg.vocab_size;
 
   for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
+    const bool q = (quantize_mask >> i) & 1u;
     uint8_t* p = nullptr;
-    int rc = dev_alloc(c, c->w_allocs, &p, std::max<size_t>(sizes[i], 16));
+    int rc = dev_alloc(c, c->w_allocs, &p, std::max<size_t>(q ? expect[i] : sizes[i], 16));
     if (rc) return rc;
-    if (sizes[i]) ESM_CUDA(cudaMemcpy(p, tensors[i], sizes[i], cudaMemcpyHostToDevice));
+    if (q) {
+      // FP32 staging on the device, quantized into place (load time only).
+      std::vector<void*> tmp;
+      float* f = nullptr;
+      rc = dev_alloc(c, tmp, &f, sizes[i] / 4);
+      if (rc) return rc;
+      cudaError_t e = cudaMemcpyAsync(f, tensors[i], sizes[i], cudaMemcpyHostToDevice, c->stream);
+      if (e == cudaSuccess) e = esm::launch_quantize(dtype, f, static_cast<int64_t>(sizes[i] / 128), p, c->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+      free_list(tmp);
+      if (e != cudaSuccess) return fail(c, ESM_ECUDA, std::string("device quantization: ") + cudaGetErrorString(e));
+    } else if (sizes[i]) {
+      // On the context's stream, so the conversions enqueued below on that (non-blocking) stream
+      // are ordered after the copy: a cudaMemcpy from pageable memory may return before its DMA
+      // into device memory has finished.
+      ESM_CUDA(cudaMemcpyAsync(p, tensors[i], sizes[i], cudaMemcpyHostToDevice, c->stream));
+    }
     c->w[i] = p;
   }
   c->classifier_floats = static_cast<int64_t>(sizes[19] / 4);
@@ -280,7 +311,8 @@ int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* con
     }
     int rc = dev_alloc(c, c->w_allocs, &c->bqkv, hb.size());
     if (rc) return rc;
-    ESM_CUDA(cudaMemcpy(c->bqkv, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice));
+    ESM_CUDA(cudaMemcpyAsync(c->bqkv, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    ESM_CUDA(cudaStreamSynchronize(c->stream));  // hb is a local staging vector
   }
   if (dtype == ESM_DTYPE_Q8_0) {
     int rc = dev_alloc(c, c->w_allocs, &c->emb_f32, static_cast<size_t>(V * d));
@@ -380,12 +412,15 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   }
   if (rc) return rc;
   // Stale rows past T are read by the GEMM A-loads of a partial last tile; keep them finite.
-  ESM_CUDA(cudaMemset(c->xn, 0, rows * d * 2));
-  ESM_CUDA(cudaMemset(c->ao, 0, rows * d * 2));
-  ESM_CUDA(cudaMemset(c->hb, 0, rows * F * 2));
+  // Everything the forward kernels read is written on the context's (non-blocking) stream, which
+  // the legacy default stream of cudaMemset / cudaMemcpy does not order against.
+  ESM_CUDA(cudaMemsetAsync(c->xn, 0, rows * d * 2, c->stream));
+  ESM_CUDA(cudaMemsetAsync(c->ao, 0, rows * d * 2, c->stream));
+  ESM_CUDA(cudaMemsetAsync(c->hb, 0, rows * F * 2, c->stream));
   {
     std::vector<float2> rt = rope_table(max_len, static_cast<int>(d / H));
-    ESM_CUDA(cudaMemcpy(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    ESM_CUDA(cudaMemcpyAsync(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
+    ESM_CUDA(cudaStreamSynchronize(c->stream));  // rt is a local staging vector
   }
   ESM_CUDA(cudaMallocHost(&c->h_cu, sizeof(int32_t) * (max_seqs + 1)));
   ESM_CUDA(cudaMallocHost(&c->h_work, sizeof(int2) * c->work_cap));
@@ -739,7 +774,8 @@ int check_device_word(esm_ctx* c) {
   int h = 0;
   ESM_CUDA(cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (h != 0) {
-    cudaMemset(c->d_err, 0, sizeof(int));
+    cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream);
+    cudaStreamSynchronize(c->stream);
     return fail(c, ESM_ETIMEOUT, "a device-side bounded wait gave up (code " + std::to_string(h) + ")");
   }
   return ESM_OK;
@@ -835,7 +871,9 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(2, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+      cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
+      cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream) != cudaSuccess ||
+      cudaStreamSynchronize(c->stream) != cudaSuccess) {
     delete c;
     return ESM_ECUDA;
   }
@@ -873,15 +911,30 @@ int esm_load_host(esm_ctx* c, const esm_config* cfg, int32_t dtype, const void* 
   return load_host_impl(c, *cfg, dtype, tensors, sizes);
 }
 
-int esm_load_file(esm_ctx* c, const char* path, const esm_config* cfg_in) {
-  if (!c || !path) return fail(c, ESM_EINVAL, "null argument");
-  std::lock_guard<std::mutex> lk(c->mu);
+namespace {
+
+// Reads a CODQ or header-less weight file into host memory and splits it into the 20 tensors
+// (EsmWeights{,Q8,Q4}::from_file, src/lib.rs:310-547, 744-830, 1156-1242).
+struct WeightFile {
+  esm_config cfg{};
+  int dtype = ESM_DTYPE_FP32;
+  const void* ptr[ESM_NUM_TENSORS] = {};
+  size_t sizes[ESM_NUM_TENSORS] = {};
+  std::vector<uint8_t> buf;
+  std::vector<float> reordered;
+};
+
+int read_weight_file(esm_ctx* c, const char* path, const esm_config* cfg_in, WeightFile& wf) {
+  esm_config& cfg = wf.cfg;
+  int& dtype = wf.dtype;
+  const void** ptr = wf.ptr;
+  size_t* sizes = wf.sizes;
+  std::vector<uint8_t>& buf = wf.buf;
+  std::vector<float>& reordered = wf.reordered;
   std::ifstream f(path, std::ios::binary | std::ios::ate);
   if (!f) return fail(c, ESM_EIO, std::string("cannot open ") + path);
   const uint64_t file_len = static_cast<uint64_t>(f.tellg());
   f.seekg(0);
-  esm_config cfg{};
-  int dtype = ESM_DTYPE_FP32;
   uint64_t start = 0;
   CodqHeader h{};
   const bool has_header = file_len >= 64 && read_exact(f, &h, 64) && std::memcmp(h.magic, "CODQ", 4) == 0;
@@ -905,16 +958,13 @@ int esm_load_file(esm_ctx* c, const char* path, const esm_config* cfg_in) {
     else if (path_hint(p, "q8")) dtype = ESM_DTYPE_Q8_0;
   }
   const uint64_t remaining = file_len - start;
-  std::vector<uint8_t> buf(remaining);
+  buf.resize(remaining);
   f.clear();
   f.seekg(static_cast<std::streamoff>(start));
   if (!read_exact(f, buf.data(), remaining)) return fail(c, ESM_EIO, "short read");
 
   int64_t sz[ESM_NUM_TENSORS];
   esm::tensor_layout(cfg, dtype, sz);
-  const void* ptr[ESM_NUM_TENSORS];
-  size_t sizes[ESM_NUM_TENSORS];
-  std::vector<float> reordered;
   if (dtype == ESM_DTYPE_FP32) {
     if (remaining % 4) return fail(c, ESM_EFORMAT, "Unaligned trailing bytes: not a multiple of 4");
     const int64_t floats = static_cast<int64_t>(remaining / 4);
@@ -1002,7 +1052,48 @@ int esm_load_file(esm_ctx* c, const char* path, const esm_config* cfg_in) {
     ptr[19] = buf.data() + off;
     sizes[19] = static_cast<size_t>(rest);
   }
-  return load_host_impl(c, cfg, dtype, ptr, sizes);
+  return ESM_OK;
+}
+
+}  // namespace
+
+int esm_load_file(esm_ctx* c, const char* path, const esm_config* cfg_in) {
+  if (!c || !path) return fail(c, ESM_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  WeightFile wf;
+  const int rc = read_weight_file(c, path, cfg_in, wf);
+  if (rc) return rc;
+  return load_host_impl(c, wf.cfg, wf.dtype, wf.ptr, wf.sizes);
+}
+
+int esm_load_file_quantized(esm_ctx* c, const char* path, const esm_config* cfg_in, int32_t dtype) {
+  if (!c || !path) return fail(c, ESM_EINVAL, "null argument");
+  if (dtype != ESM_DTYPE_Q8_0 && dtype != ESM_DTYPE_Q4_0) return fail(c, ESM_EINVAL, "dtype must be Q8_0 or Q4_0");
+  std::lock_guard<std::mutex> lk(c->mu);
+  WeightFile wf;
+  const int rc = read_weight_file(c, path, cfg_in, wf);
+  if (rc) return rc;
+  // As in load_model_weights, the requested type applies to FP32 files; a Q8_0 / Q4_0 file loads
+  // as it is stored.
+  if (wf.dtype != ESM_DTYPE_FP32) return load_host_impl(c, wf.cfg, wf.dtype, wf.ptr, wf.sizes);
+  return load_host_impl(c, wf.cfg, dtype, wf.ptr, wf.sizes, quantized_tensors(dtype));
+}
+
+int esm_load_host_quantized(esm_ctx* c, const esm_config* cfg, int32_t dtype, const void* const* tensors,
+                            const size_t* sizes) {
+  if (!c || !cfg || !tensors || !sizes) return fail(c, ESM_EINVAL, "null argument");
+  if (dtype != ESM_DTYPE_Q8_0 && dtype != ESM_DTYPE_Q4_0) return fail(c, ESM_EINVAL, "dtype must be Q8_0 or Q4_0");
+  std::lock_guard<std::mutex> lk(c->mu);
+  return load_host_impl(c, *cfg, dtype, tensors, sizes, quantized_tensors(dtype));
+}
+
+int esm_quantize_device(int32_t dtype, const float* d_src, int64_t n, void* d_dst, void* stream) {
+  if (!d_src || !d_dst || n < 0 || n % 32) return ESM_EINVAL;
+  if (dtype != ESM_DTYPE_Q8_0 && dtype != ESM_DTYPE_Q4_0) return ESM_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(d_src) & 15) || (reinterpret_cast<uintptr_t>(d_dst) & 3)) return ESM_EINVAL;
+  const cudaError_t e = esm::launch_quantize(dtype, d_src, n / 32, static_cast<uint8_t*>(d_dst),
+                                             static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ESM_OK : ESM_ECUDA;
 }
 
 int esm_set_contact_head(esm_ctx* c, const float* w, int32_t nw, float b) {
@@ -1014,7 +1105,8 @@ int esm_set_contact_head(esm_ctx* c, const float* w, int32_t nw, float b) {
                                    std::to_string(c->cfg.n_layers * c->cfg.n_heads) + " weights");
   ESM_CUDA(cudaSetDevice(c->device));
   if (!c->d_ch_w) ESM_CUDA(cudaMalloc(&c->d_ch_w, sizeof(float) * nw));
-  ESM_CUDA(cudaMemcpy(c->d_ch_w, w, sizeof(float) * nw, cudaMemcpyHostToDevice));
+  ESM_CUDA(cudaMemcpyAsync(c->d_ch_w, w, sizeof(float) * nw, cudaMemcpyHostToDevice, c->stream));
+  ESM_CUDA(cudaStreamSynchronize(c->stream));
   c->ch_b = b;
   c->has_ch = true;
   return ESM_OK;

@@ -174,8 +174,10 @@ void quantize_q4(const float* src, int64_t n, uint8_t* dst) {
       uint8_t* o = dst + b * 20;
       std::memcpy(o, &d, 4);
       for (int j = 0; j < 16; ++j) {
-        int32_t lo = sat_i32(std::roundf(x[j] * id)) + 8;
-        int32_t hi = sat_i32(std::roundf(x[j + 16] * id)) + 8;
+        // `as i32 + 8` wraps like the reference's release build (reachable only when 1/d
+        // overflows, i.e. for blocks whose largest magnitude is subnormal).
+        int32_t lo = static_cast<int32_t>(static_cast<uint32_t>(sat_i32(std::roundf(x[j] * id))) + 8u);
+        int32_t hi = static_cast<int32_t>(static_cast<uint32_t>(sat_i32(std::roundf(x[j + 16] * id))) + 8u);
         lo = std::min(std::max(lo, 0), 15);
         hi = std::min(std::max(hi, 0), 15);
         o[4 + j] = static_cast<uint8_t>((lo & 0x0F) | ((hi & 0x0F) << 4));

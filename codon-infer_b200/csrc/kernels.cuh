@@ -95,6 +95,9 @@ cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_
                                  int poly_eighths, cudaStream_t s);
 // Same with 32-key K/V tiles and two score buffers per query tile (attention_tc3.cu, head_dim 64 or
 // 32): tm_kv32 boxes are 32 rows x head_dim columns (128- or 64-byte swizzle, as tm_q).
+// BlockQ8_0 / BlockQ4_0 quantization of nblocks x 32 FP32 values on the device (quantize.cu);
+// dtype 1 = Q8_0, 2 = Q4_0; src 16-byte aligned, dst 4-byte aligned.
+cudaError_t launch_quantize(int dtype, const float* src, int64_t nblocks, uint8_t* dst, cudaStream_t s);
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s);
 

@@ -104,6 +104,9 @@ def lib() -> ctypes.CDLL:
             "esm_ctx_destroy": [vp],
             "esm_load_file": [vp, ctypes.c_char_p, vp],
             "esm_load_host": [vp, vp, i32, vp, vp],
+            "esm_load_host_quantized": [vp, vp, i32, vp, vp],
+            "esm_load_file_quantized": [vp, ctypes.c_char_p, vp, i32],
+            "esm_quantize_device": [i32, vp, i64, vp, vp],
             "esm_set_contact_head": [vp, vp, i32, f32],
             "esm_reserve": [vp, i32, i32, i32, i32],
             "esm_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
@@ -151,6 +154,13 @@ def quantize_q4(x) -> np.ndarray:
     out = np.empty(x.size // 32 * Q4_BLOCK_BYTES, dtype=np.uint8)
     _check(lib().esm_quantize_q4(_p(x), x.size, _p(out)), "esm_quantize_q4")
     return out
+
+
+def quantize_device(dtype: int, d_src: int, n: int, d_dst: int, stream: int = 0) -> None:
+    """esm_quantize_device on raw device pointers (e.g. torch tensors' data_ptr())."""
+    rc = lib().esm_quantize_device(dtype, d_src, n, d_dst, stream or None)
+    if rc != ESM_OK:
+        raise EsmError(rc, "esm_quantize_device")
 
 
 def tokenize(seq: str) -> np.ndarray:
@@ -293,6 +303,23 @@ class Model:
         c = cfg.c_struct()
         self._chk(lib().esm_load_host(self._ctx, ctypes.byref(c), dtype, ptrs, sizes), "esm_load_host")
         self.cfg = cfg
+
+    def load_tensors_quantized(self, cfg: EsmConfig, dtype: int, fp32_tensors: dict) -> None:
+        """FP32 tensors (synth_fp32_tensors layout) quantized to `dtype` on the device while loading
+        (EsmWeights::quantize_q8 / quantize_q4)."""
+        arrs = [np.ascontiguousarray(fp32_tensors[n], dtype=np.float32) for n in TENSOR_NAMES]
+        ptrs = (ctypes.c_void_p * 20)(*[a.ctypes.data if a.size else None for a in arrs])
+        sizes = (ctypes.c_size_t * 20)(*[a.nbytes for a in arrs])
+        c = cfg.c_struct()
+        self._chk(lib().esm_load_host_quantized(self._ctx, ctypes.byref(c), dtype, ptrs, sizes),
+                  "esm_load_host_quantized")
+        self.cfg = cfg
+
+    def load_file_quantized(self, path: str, dtype: int, cfg: EsmConfig | None = None) -> None:
+        c = cfg.c_struct() if cfg else None
+        self._chk(lib().esm_load_file_quantized(self._ctx, str(path).encode(), ctypes.byref(c) if c else None, dtype),
+                  "esm_load_file_quantized")
+        self.cfg = cfg or detect_file(path)[0]
 
     def load_file(self, path: str, cfg: EsmConfig | None = None) -> None:
         c = cfg.c_struct() if cfg else None

@@ -78,6 +78,11 @@ int esm_config_detect_file(const char* path, esm_config* out, int32_t* dtype);
 int esm_quantize_q8(const float* src, int64_t n, void* dst);
 /* quantize_slice_to_q4 / BlockQ4_0::quantize, src/lib.rs:1054-1088: dst holds n/32 x 20 bytes. */
 int esm_quantize_q4(const float* src, int64_t n, void* dst);
+/* The same two quantizers on device memory (dtype ESM_DTYPE_Q8_0 or ESM_DTYPE_Q4_0): d_src holds
+ * n FP32 values (n % 32 == 0, 16-byte aligned), d_dst receives the n/32 blocks (4-byte aligned),
+ * byte-identical to esm_quantize_q8/q4. Enqueued on `stream` (a cudaStream_t; NULL = the legacy
+ * default stream); the caller synchronises. */
+int esm_quantize_device(int32_t dtype, const float* d_src, int64_t n, void* d_dst, void* stream);
 
 /* Tokenizer::encode, src/lib.rs:6511-6521: <cls> + ids + <eos>; returns ESM_ECAPACITY if the
  * sequence needs more than `cap` tokens. *n_out receives the token count. */
@@ -96,6 +101,17 @@ int esm_load_file(esm_ctx* ctx, const char* path, const esm_config* cfg);
 /* Upload weights from host memory: tensors[i] / sizes[i] (bytes) in the order above. */
 int esm_load_host(esm_ctx* ctx, const esm_config* cfg, int32_t dtype, const void* const* tensors,
                   const size_t* sizes);
+
+/* EsmWeights::quantize_q8 / quantize_q4 (src/lib.rs:559-607) done on the device while uploading:
+ * tensors / sizes are an FP32 weight set (the ESM_DTYPE_FP32 layout); the six matrices of every
+ * layer, and for Q8_0 the token embedding, are quantized on the GPU into a `dtype` (Q8_0 or Q4_0)
+ * model, block for block identical to the host quantizers. */
+int esm_load_host_quantized(esm_ctx* ctx, const esm_config* cfg, int32_t dtype, const void* const* tensors,
+                            const size_t* sizes);
+
+/* load_model_weights with QuantizationMode::Q8_0 / Q4_0 (src/main.rs:137-244): an FP32 weight
+ * file is quantized on the device while loading; a Q8_0 / Q4_0 file loads as it is stored. */
+int esm_load_file_quantized(esm_ctx* ctx, const char* path, const esm_config* cfg, int32_t dtype);
 
 /* Contact regression head (EsmConfig::contact_head_weights, src/lib.rs:154-177): w has
  * n_layers * n_heads entries (layer-major), b is the bias. Required before contacts are asked for. */
