@@ -124,6 +124,8 @@ struct esm_ctx {
   size_t ev_used = 0;
   std::vector<ProfRec> prof_recs;
   // host-API staging (grows on demand)
+  uint64_t* d_rank = nullptr;  // contact-pair ranking scratch (grown on demand)
+  size_t rank_cap = 0;
   int32_t* d_padded_tokens = nullptr;
   size_t padded_tok_cap = 0;
   float* d_padded_out = nullptr;
@@ -891,6 +893,7 @@ int esm_ctx_destroy(esm_ctx* c) {
     free_list(c->ws_allocs);
     free_pinned(c);
     if (c->d_ch_w) cudaFree(c->d_ch_w);
+    if (c->d_rank) cudaFree(c->d_rank);
     if (c->d_padded_tokens) cudaFree(c->d_padded_tokens);
     if (c->d_padded_out) cudaFree(c->d_padded_out);
     if (c->d_dms) cudaFree(c->d_dms);
@@ -1085,6 +1088,69 @@ int esm_load_host_quantized(esm_ctx* c, const esm_config* cfg, int32_t dtype, co
   if (dtype != ESM_DTYPE_Q8_0 && dtype != ESM_DTYPE_Q4_0) return fail(c, ESM_EINVAL, "dtype must be Q8_0 or Q4_0");
   std::lock_guard<std::mutex> lk(c->mu);
   return load_host_impl(c, *cfg, dtype, tensors, sizes, quantized_tensors(dtype));
+}
+
+int esm_contact_top_pairs(esm_ctx* c, const float* d_map, int32_t n, const char* seq, int32_t min_separation,
+                          int32_t max_k, float top_l_factor, int32_t* pos1, int32_t* pos2, float* score,
+                          int32_t* n_out, float* cys_enrichment) {
+  if (!c || !d_map || !seq || !pos1 || !pos2 || !score || !n_out || !cys_enrichment)
+    return fail(c, ESM_EINVAL, "null argument");
+  // compute_pipeline_contacts_parallel asserts n >= 4 (src/pipeline.rs:421).
+  if (n < 4) return fail(c, ESM_EINVAL, "Sequence too short for contact prediction");
+  if (min_separation < 0) return fail(c, ESM_EINVAL, "min_separation must be >= 0");
+  std::lock_guard<std::mutex> lk(c->mu);
+  // Candidate and Cys-Cys pair counts (src/pipeline.rs:454-477).
+  int64_t total = 0;
+  for (int64_t i = 0; i < n; ++i) total += std::max<int64_t>(0, n - (i + min_separation));
+  std::vector<int32_t> cys;
+  for (int32_t i = 0; i < n; ++i)
+    if (seq[i] == 'C') cys.push_back(i);
+  int64_t cys_pairs = 0;
+  for (size_t a = 0; a < cys.size(); ++a)
+    for (size_t b = a + 1; b < cys.size(); ++b)
+      if (cys[b] >= cys[a] + min_separation) ++cys_pairs;
+  // top_k (src/pipeline.rs:480-485): max_k, else round(n * top_l_factor) clamped to [5, 50].
+  int64_t k;
+  if (max_k >= 0) {
+    k = std::min<int64_t>(max_k, total);
+  } else {
+    const float r = std::round(static_cast<float>(n) * top_l_factor);  // f32 product, half away from zero
+    const int64_t rk = (r != r || r <= 0.0f) ? 0 : (r >= 9.2e18f ? INT64_MAX : static_cast<int64_t>(r));
+    k = std::min<int64_t>(std::min<int64_t>(std::max<int64_t>(rk, 5), 50), total);
+  }
+  if (k > 4096) return fail(c, ESM_EINVAL, "at most 4096 top pairs are returned");
+  int32_t top_cys = 0;
+  if (k > 0) {
+    const size_t need = static_cast<size_t>(esm::contact_rank_scratch_keys(n, static_cast<int>(k))) + 4096;
+    ESM_CUDA(cudaSetDevice(c->device));
+    if (need > c->rank_cap) {
+      if (c->d_rank) cudaFree(c->d_rank);
+      c->d_rank = nullptr;
+      c->rank_cap = 0;
+      ESM_CUDA(cudaMalloc(&c->d_rank, need * sizeof(uint64_t)));
+      c->rank_cap = need;
+    }
+    uint64_t* out_keys = c->d_rank + (need - 4096);
+    ESM_CUDA(esm::launch_contact_rank(d_map, n, min_separation, static_cast<int>(k), c->d_rank, out_keys, c->stream));
+    std::vector<uint64_t> keys(static_cast<size_t>(k));
+    ESM_CUDA(cudaMemcpyAsync(keys.data(), out_keys, keys.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost, c->stream));
+    ESM_CUDA(cudaStreamSynchronize(c->stream));
+    for (int64_t t = 0; t < k; ++t) {
+      const uint32_t flat = static_cast<uint32_t>(keys[t]);
+      const uint32_t asc = ~static_cast<uint32_t>(keys[t] >> 32);
+      const uint32_t u = (asc & 0x80000000u) ? (asc & 0x7FFFFFFFu) : ~asc;
+      pos1[t] = static_cast<int32_t>(flat / static_cast<uint32_t>(n));
+      pos2[t] = static_cast<int32_t>(flat % static_cast<uint32_t>(n));
+      std::memcpy(&score[t], &u, 4);
+      if (seq[pos1[t]] == 'C' && seq[pos2[t]] == 'C') ++top_cys;
+    }
+  }
+  *n_out = static_cast<int32_t>(k);
+  // Enrichment in f32 as the reference computes it (src/pipeline.rs:487-503).
+  const float top_density = k > 0 ? static_cast<float>(top_cys) / static_cast<float>(k) : 0.0f;
+  const float bg_density = total > 0 ? static_cast<float>(cys_pairs) / static_cast<float>(total) : 0.05f;
+  *cys_enrichment = bg_density > 0.0f ? top_density / bg_density : 1.0f;
+  return ESM_OK;
 }
 
 int esm_quantize_device(int32_t dtype, const float* d_src, int64_t n, void* d_dst, void* stream) {

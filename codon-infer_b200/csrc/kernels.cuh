@@ -98,6 +98,11 @@ cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_
 // BlockQ8_0 / BlockQ4_0 quantization of nblocks x 32 FP32 values on the device (quantize.cu);
 // dtype 1 = Q8_0, 2 = Q4_0; src 16-byte aligned, dst 4-byte aligned.
 cudaError_t launch_quantize(int dtype, const float* src, int64_t nblocks, uint8_t* dst, cudaStream_t s);
+// Top-k ranking of contact pairs (contact_rank.cu): keys of the first k (<= 4096) candidate pairs
+// (j >= i + min_sep) of the n x n map in the reference's order, into out_keys (ascending).
+int64_t contact_rank_scratch_keys(int n, int k);
+cudaError_t launch_contact_rank(const float* map, int n, int min_sep, int k, uint64_t* scratch, uint64_t* out_keys,
+                                cudaStream_t s);
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s);
 

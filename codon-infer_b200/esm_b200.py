@@ -107,6 +107,7 @@ def lib() -> ctypes.CDLL:
             "esm_load_host_quantized": [vp, vp, i32, vp, vp],
             "esm_load_file_quantized": [vp, ctypes.c_char_p, vp, i32],
             "esm_quantize_device": [i32, vp, i64, vp, vp],
+            "esm_contact_top_pairs": [vp, vp, i32, ctypes.c_char_p, i32, i32, f32, vp, vp, vp, vp, vp],
             "esm_set_contact_head": [vp, vp, i32, f32],
             "esm_reserve": [vp, i32, i32, i32, i32],
             "esm_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
@@ -320,6 +321,23 @@ class Model:
         self._chk(lib().esm_load_file_quantized(self._ctx, str(path).encode(), ctypes.byref(c) if c else None, dtype),
                   "esm_load_file_quantized")
         self.cfg = cfg or detect_file(path)[0]
+
+    def contact_top_pairs(self, d_map: int, n: int, seq: str, min_separation: int = 6,
+                          max_k: int | None = None, top_l_factor: float = 1.0) -> dict:
+        """Ranked contact pairs of one sequence's n x n map in device memory (a device pointer), as
+        compute_pipeline_contacts_parallel ranks them; see esm_contact_top_pairs."""
+        cap = 4096
+        pos1 = np.zeros(cap, dtype=np.int32)
+        pos2 = np.zeros(cap, dtype=np.int32)
+        score = np.zeros(cap, dtype=np.float32)
+        n_out = ctypes.c_int32(0)
+        enr = ctypes.c_float(0.0)
+        self._chk(lib().esm_contact_top_pairs(self._ctx, d_map, n, seq.encode(), min_separation,
+                                              -1 if max_k is None else max_k, top_l_factor, _p(pos1), _p(pos2),
+                                              _p(score), ctypes.byref(n_out), ctypes.byref(enr)),
+                  "esm_contact_top_pairs")
+        k = n_out.value
+        return {"pos1": pos1[:k], "pos2": pos2[:k], "score": score[:k], "cys_enrichment": enr.value}
 
     def load_file(self, path: str, cfg: EsmConfig | None = None) -> None:
         c = cfg.c_struct() if cfg else None

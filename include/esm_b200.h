@@ -88,6 +88,21 @@ int esm_quantize_device(int32_t dtype, const float* d_src, int64_t n, void* d_ds
  * sequence needs more than `cap` tokens. *n_out receives the token count. */
 int esm_tokenize(const char* seq, int32_t* out, int32_t cap, int32_t* n_out);
 
+/* ---- contact post-processing ------------------------------------------------------------ */
+
+/* The pair ranking and Cys enrichment of compute_pipeline_contacts_parallel (src/pipeline.rs:410-512)
+ * on a contact map in device memory (one sequence's n x n probabilities, row-major, e.g. its slice of
+ * esm_forward_device's contacts; n = residues = L - 2 >= 4): the pairs (i, j) with
+ * j >= i + min_separation, in descending probability with ties in (i, j) order (the reference's
+ * stable sort), the first k of them into pos1/pos2/score (host arrays of k entries; *n_out = k),
+ * where k = min(max_k, #candidates) for max_k >= 0, else round(n * top_l_factor) clamped to [5, 50]
+ * and to #candidates; k may not exceed 4096. seq holds the n residue letters (host memory);
+ * *cys_enrichment = (Cys-Cys share of the k pairs) / (Cys-Cys share of all candidates), computed in
+ * f32 as the reference does. The map is not copied to the host. */
+int esm_contact_top_pairs(esm_ctx* ctx, const float* d_map, int32_t n, const char* seq, int32_t min_separation,
+                          int32_t max_k, float top_l_factor, int32_t* pos1, int32_t* pos2, float* score,
+                          int32_t* n_out, float* cys_enrichment);
+
 /* ---- context ------------------------------------------------------------------------------ */
 
 int esm_ctx_create(int32_t device, esm_ctx** out);
