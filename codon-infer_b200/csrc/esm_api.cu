@@ -1255,6 +1255,96 @@ int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32
   return check_device_word(c);
 }
 
+int esm_dms_wildtype_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, int32_t stride,
+                              float* deltas, float* entropy) {
+  if (!c || !residues || !deltas || !entropy) return fail(c, ESM_EINVAL, "null argument");
+  if (n <= 0) return fail(c, ESM_EINVAL, "Sequence cannot be empty");
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (!c->loaded) return fail(c, ESM_EINVAL, "no weights loaded");
+  if (c->cap_tokens == 0) return fail(c, ESM_EINVAL, "call esm_reserve before the first forward");
+  ESM_CUDA(cudaSetDevice(c->device));
+  cudaStream_t s = c->stream;
+  const int max_len = c->cfg.max_seq_len;
+  // Window arithmetic of run_pipeline_dms_with_mode (src/pipeline.rs:88-94, 176-291).
+  const int W = (n <= window_size || window_size == 0) ? std::min(n, max_len) : std::min(window_size, max_len);
+  if (W + 2 > c->cap_len)
+    return fail(c, ESM_ECAPACITY, "window of " + std::to_string(W + 2) + " tokens exceeds max_len " +
+                                      std::to_string(c->cap_len));
+  if (W + 2 > c->cap_tokens) return fail(c, ESM_ECAPACITY, "window exceeds the reserved token capacity");
+  // Windows [w_start, w_end) and the positions each one scores: one window when the sequence fits,
+  // else windows `step` apart (stride when 0 < stride <= W, else W / 2), the last one ending at n;
+  // every position is scored by the first window that covers it.
+  struct Win { int start, end, first; };
+  std::vector<Win> wins;
+  if (n <= W) {
+    wins.push_back({0, n, 0});
+  } else {
+    const int step = (stride > 0 && stride <= W) ? stride : std::max(W / 2, 1);
+    int covered = 0, w_start = 0;
+    while (covered < n) {
+      const int w_end = std::min(w_start + W, n);
+      wins.push_back({w_start, w_end, covered});
+      covered = w_end;
+      if (w_end >= n) break;
+      w_start = std::min(w_start + step, n - W);
+    }
+  }
+  // Staging: tok_row[n] | wt_tok[n] | deltas[20 n] | entropy[n]
+  const size_t need = static_cast<size_t>(n) * (2 * 4 + 21 * 4);
+  if (need > c->dms_cap) {
+    if (c->d_dms) cudaFree(c->d_dms);
+    c->d_dms = nullptr;
+    c->dms_cap = 0;
+    ESM_CUDA(cudaMalloc(&c->d_dms, need));
+    c->dms_cap = need;
+  }
+  int32_t* d_row = static_cast<int32_t*>(c->d_dms);
+  int32_t* d_wt = d_row + n;
+  float* d_delta = reinterpret_cast<float*>(d_wt + n);
+  float* d_ent = d_delta + static_cast<size_t>(20) * n;
+  std::vector<int32_t> toks, cu{0}, rows, wts;
+  int p0 = 0;  // first position scored by the current batch
+  for (size_t w = 0; w <= wins.size(); ++w) {
+    const bool flush = (w == wins.size()) || static_cast<int>(cu.size()) - 1 == c->cap_seqs ||
+                       cu.back() + (wins[w].end - wins[w].start) + 2 > c->cap_tokens;
+    if (flush && cu.size() > 1) {
+      // One batch of windows through the forward, then score the rows of their positions.
+      const int B = static_cast<int>(cu.size()) - 1;
+      const int nr = static_cast<int>(rows.size());
+      int rc = validate_call(c, cu.data(), B, false);
+      if (rc) return rc;
+      ESM_CUDA(cudaMemcpyAsync(c->tokens, toks.data(), toks.size() * 4, cudaMemcpyHostToDevice, s));
+      ESM_CUDA(cudaMemcpyAsync(d_row + p0, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, s));
+      ESM_CUDA(cudaMemcpyAsync(d_wt + p0, wts.data(), wts.size() * 4, cudaMemcpyHostToDevice, s));
+      rc = forward_impl(c, c->tokens, cu.data(), B, c->logits, nullptr, nullptr, nullptr, s);
+      if (rc) return rc;
+      ESM_CUDA(esm::launch_dms_score(c->logits, c->cfg.vocab_size, d_row + p0, d_wt + p0, nr,
+                                     d_delta + static_cast<size_t>(20) * p0, d_ent + p0, s));
+      ESM_CUDA(cudaStreamSynchronize(s));  // the host vectors are reused by the next batch
+      p0 += nr;
+      toks.clear();
+      rows.clear();
+      wts.clear();
+      cu.assign(1, 0);
+    }
+    if (w == wins.size()) break;
+    const Win& wi = wins[w];
+    const int base = cu.back();
+    toks.push_back(0);
+    for (int i = wi.start; i < wi.end; ++i) toks.push_back(residues[i]);
+    toks.push_back(2);
+    for (int p = wi.first; p < wi.end; ++p) {
+      rows.push_back(base + (p - wi.start) + 1);
+      wts.push_back(residues[p]);
+    }
+    cu.push_back(base + (wi.end - wi.start) + 2);
+  }
+  ESM_CUDA(cudaMemcpyAsync(deltas, d_delta, static_cast<size_t>(20) * n * 4, cudaMemcpyDeviceToHost, s));
+  ESM_CUDA(cudaMemcpyAsync(entropy, d_ent, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, s));
+  ESM_CUDA(cudaStreamSynchronize(s));
+  return check_device_word(c);
+}
+
 int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
                             float* entropy) {
   if (!c || !residues || !deltas || !entropy) return fail(c, ESM_EINVAL, "null argument");

@@ -114,6 +114,7 @@ def lib() -> ctypes.CDLL:
             "esm_forward_device": [vp, vp, vp, i32, vp, vp, vp, vp, vp, i32],
             "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
             "esm_dms_masked_marginal": [vp, vp, i32, i32, vp, vp],
+            "esm_dms_wildtype_marginal": [vp, vp, i32, i32, i32, vp, vp],
             "esm_check_device": [vp],
             "esm_probe_wait_timeout": [vp, i32],
             "esm_profile_enable": [vp, i32],
@@ -407,6 +408,15 @@ class Model:
         self._chk(lib().esm_forward_device(self._ctx, ptr(d_tokens), _p(cu), cu.size - 1, ptr(d_logits),
                                            ptr(d_hidden), ptr(d_contacts), ptr(d_layer_hidden), s, int(sync)),
                   "esm_forward_device")
+
+    def dms_wildtype_marginal(self, residues, window_size: int = 0, stride: int = 0):
+        """Wild-type-marginal scan (no masking, sliding windows); same outputs as dms_masked_marginal."""
+        r = np.ascontiguousarray(residues, dtype=np.int32)
+        deltas = np.empty((r.size, 20), dtype=np.float32)
+        ent = np.empty(r.size, dtype=np.float32)
+        self._chk(lib().esm_dms_wildtype_marginal(self._ctx, _p(r), r.size, window_size, stride, _p(deltas),
+                                                  _p(ent)), "esm_dms_wildtype_marginal")
+        return deltas, ent
 
     def dms_masked_marginal(self, residues, window_size: int = 0):
         """Masked-marginal deep mutational scan of one sequence (residue token ids, no <cls>/<eos>).

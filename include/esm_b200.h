@@ -173,6 +173,15 @@ int esm_forward_device(esm_ctx* ctx, const int32_t* d_tokens, const int32_t* h_c
 int esm_dms_masked_marginal(esm_ctx* ctx, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
                             float* entropy);
 
+/* The same scan in wild-type-marginal mode (DmsScoringMode::WildtypeMarginal, src/pipeline.rs:176-291):
+ * no masking; the whole sequence is one forward when it fits the window (window_size semantics as
+ * above), otherwise windows of that size `stride` residues apart (stride in (0, window], else half a
+ * window), the last one ending at the sequence end, and every position is scored from the first
+ * window that covers it. deltas / entropy as above; all windows run as batches of independent
+ * sequences. Outputs are HOST buffers. */
+int esm_dms_wildtype_marginal(esm_ctx* ctx, const int32_t* residues, int32_t n, int32_t window_size, int32_t stride,
+                              float* deltas, float* entropy);
+
 /* matmul_tiled_{fp32,q8,q4}_parallel (src/lib.rs:4803-4827, 4870-4894, 4937-4961) on the GPU, from
  * HOST buffers: out[p, i] = sum_k W[i, k] * x[p, k] + bias[i] for p < seq_len, i < out_dim.
  * w is FP32 [out_dim, in_dim] or rows of BlockQ8_0 / BlockQ4_0 (dtype); x is FP32 [seq_len, in_dim];
