@@ -239,7 +239,7 @@ uint32_t quantized_tensors(int dtype) {
 int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* const* tensors, const size_t* sizes,
                    uint32_t quantize_mask = 0) {
   std::string why;
-  if (dtype < 0 || dtype > 2) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0 or Q4_0");
+  if (dtype < 0 || dtype > 3) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0, Q4_0 or Q3_LUT");
   if (!shape_supported(cfg, &why)) return fail(c, ESM_EINVAL, "unsupported model shape: " + why);
   int64_t expect[ESM_NUM_TENSORS];
   esm::tensor_layout(cfg, dtype, expect);
@@ -584,7 +584,8 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   const float* lnf_w = static_cast<const float*>(c->w[17]);
   const float* lnf_b = static_cast<const float*>(c->w[18]);
   const int64_t dd = static_cast<int64_t>(d) * d, fd = static_cast<int64_t>(F) * d;
-  const int64_t mat_b = esm::matrix_bytes(c->dtype, dd), fc_b = esm::matrix_bytes(c->dtype, fd);
+  const int dt_mat = esm::matrix_dtype(c->dtype, 3), dt_fc = esm::matrix_dtype(c->dtype, 13);
+  const int64_t mat_b = esm::matrix_bytes(dt_mat, dd), fc_b = esm::matrix_bytes(dt_fc, fd);
 
   ESM_CUDA(esm::launch_seq_setup(d_tokens, c->cu, B, c->pos, c->seq_of, c->escale, s));
   const double rowb = static_cast<double>(T) * d;
@@ -645,7 +646,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
 
   for (int l = 0; l < nl; ++l) {
     esm::LayerSrc src{};
-    src.dtype = c->dtype;
+    for (int m = 0; m < 6; ++m) src.dtype[m] = m < 4 ? dt_mat : dt_fc;
     src.w[0] = static_cast<const uint8_t*>(c->w[3]) + l * mat_b;
     src.w[1] = static_cast<const uint8_t*>(c->w[5]) + l * mat_b;
     src.w[2] = static_cast<const uint8_t*>(c->w[7]) + l * mat_b;
@@ -850,6 +851,12 @@ int esm_quantize_q4(const float* src, int64_t n, void* dst) {
   return ESM_OK;
 }
 
+int esm_quantize_q3(const float* src, int64_t n, void* dst) {
+  if (!src || !dst || n < 0 || n % 32) return ESM_EINVAL;
+  esm::quantize_q3(src, n, static_cast<uint8_t*>(dst));
+  return ESM_OK;
+}
+
 int esm_tokenize(const char* seq, int32_t* out, int32_t cap, int32_t* n_out) {
   if (!seq || !n_out || (!out && cap > 0)) return ESM_EINVAL;
   return esm::tokenize(seq, out, cap, n_out);
@@ -946,7 +953,7 @@ int read_weight_file(esm_ctx* c, const char* path, const esm_config* cfg_in, Wei
     if (!why.empty()) return fail(c, ESM_EFORMAT, why);
     esm::config_preset(static_cast<int>(h.arch), &cfg);
     dtype = static_cast<int>(h.dtype);
-    if (dtype > ESM_DTYPE_Q4_0) return fail(c, ESM_EFORMAT, "unsupported CODQ dtype " + std::to_string(dtype));
+    if (dtype > ESM_DTYPE_Q3_LUT) return fail(c, ESM_EFORMAT, "unsupported CODQ dtype " + std::to_string(dtype));
     start = 64;
   } else {
     if (cfg_in) {
@@ -957,7 +964,8 @@ int read_weight_file(esm_ctx* c, const char* path, const esm_config* cfg_in, Wei
     // Header-less Q8_0/Q4_0 files are recognised by name, as load_or_convert does
     // (src/lib.rs:838-856, 1250-1274); everything else is FP32.
     const std::string p(path);
-    if (path_hint(p, "q4")) dtype = ESM_DTYPE_Q4_0;
+    if (path_hint(p, "q3")) dtype = ESM_DTYPE_Q3_LUT;  // load_model_weights checks q3 first (src/main.rs:190-200)
+    else if (path_hint(p, "q4")) dtype = ESM_DTYPE_Q4_0;
     else if (path_hint(p, "q8")) dtype = ESM_DTYPE_Q8_0;
   }
   const uint64_t remaining = file_len - start;
@@ -1424,7 +1432,7 @@ int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int3
 int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,
                      int32_t out_dim, int32_t seq_len, float* out) {
   if (!c || !x || !w || !out) return fail(c, ESM_EINVAL, "null argument");
-  if (dtype < 0 || dtype > 2) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0 or Q4_0");
+  if (dtype < 0 || dtype > 3) return fail(c, ESM_EINVAL, "dtype must be FP32, Q8_0, Q4_0 or Q3_LUT");
   if (in_dim <= 0 || in_dim % 32 || out_dim <= 0 || seq_len <= 0)
     return fail(c, ESM_EINVAL, "in_dim must be a positive multiple of 32; out_dim and seq_len positive");
   std::lock_guard<std::mutex> lk(c->mu);

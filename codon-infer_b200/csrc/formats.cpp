@@ -1,6 +1,7 @@
 // Host-side weight formats of codon-infer: architecture presets, CODQ header, file-size
-// autodetection, tensor layouts of grouped_canonical_v1 / sequential_hf / CODQ files, the Q8_0 and
-// Q4_0 quantizers (bit-exact) and the tokenizer.
+// autodetection, tensor layouts of grouped_canonical_v1 / sequential_hf / CODQ files, the Q8_0,
+// Q4_0 and Q3_LUT quantizers (bit-exact; this file is compiled without floating-point
+// contraction, so every product and sum rounds on its own as in the reference) and the tokenizer.
 #include "formats.h"
 
 #include <algorithm>
@@ -85,7 +86,15 @@ std::string CodqHeader::validate(const esm_config* cfg) const {
 int64_t matrix_bytes(int dtype, int64_t elems) {
   if (dtype == ESM_DTYPE_Q8_0) return elems / 32 * 36;
   if (dtype == ESM_DTYPE_Q4_0) return elems / 32 * 20;
+  if (dtype == ESM_DTYPE_Q3_LUT) return elems / 32 * 14;
   return elems * 4;
+}
+
+int matrix_dtype(int model_dtype, int tensor) {
+  // EsmWeights::quantize_q3 (src/lib.rs:609-633): a Q3_LUT model keeps Q4_0 attention matrices and
+  // stores fc1 / fc2 (tensors 13, 15) as Q3_LUT; the other model types use one type throughout.
+  if (model_dtype == ESM_DTYPE_Q3_LUT) return (tensor == 13 || tensor == 15) ? ESM_DTYPE_Q3_LUT : ESM_DTYPE_Q4_0;
+  return model_dtype;
 }
 
 void tensor_layout(const esm_config& c, int dtype, int64_t out_bytes[ESM_NUM_TENSORS]) {
@@ -96,13 +105,13 @@ void tensor_layout(const esm_config& c, int dtype, int64_t out_bytes[ESM_NUM_TEN
   out_bytes[0] = (dtype == ESM_DTYPE_Q8_0) ? matrix_bytes(ESM_DTYPE_Q8_0, V * d) : V * d * 4;
   out_bytes[1] = vec;
   out_bytes[2] = vec;
-  for (int i : {3, 5, 7, 9}) out_bytes[i] = matrix_bytes(dtype, nl * d * d);
+  for (int i : {3, 5, 7, 9}) out_bytes[i] = matrix_bytes(matrix_dtype(dtype, i), nl * d * d);
   for (int i : {4, 6, 8, 10}) out_bytes[i] = vec;
   out_bytes[11] = vec;
   out_bytes[12] = vec;
-  out_bytes[13] = matrix_bytes(dtype, nl * F * d);
+  out_bytes[13] = matrix_bytes(matrix_dtype(dtype, 13), nl * F * d);
   out_bytes[14] = nl * F * 4;
-  out_bytes[15] = matrix_bytes(dtype, nl * d * F);
+  out_bytes[15] = matrix_bytes(matrix_dtype(dtype, 15), nl * d * F);
   out_bytes[16] = vec;
   out_bytes[17] = d * 4;
   out_bytes[18] = d * 4;
@@ -183,6 +192,131 @@ void quantize_q4(const float* src, int64_t n, uint8_t* dst) {
         o[4 + j] = static_cast<uint8_t>((lo & 0x0F) | ((hi & 0x0F) << 4));
       }
     }
+  });
+}
+
+uint16_t q3_scale_to_half(float v) {
+  // f32_to_f16, src/lib.rs:1291-1312: the exponent rebiased and the mantissa truncated; zero for
+  // f32 subnormals and for results below the half range, infinity above it, NaN payload kept.
+  uint32_t bits;
+  std::memcpy(&bits, &v, 4);
+  const uint32_t sign = (bits >> 31) & 1u, frac = bits & 0x7FFFFFu;
+  const int exp = static_cast<int>((bits >> 23) & 0xFFu);
+  if (exp == 0) return static_cast<uint16_t>(sign << 15);
+  if (exp == 0xFF) return static_cast<uint16_t>((sign << 15) | 0x7C00u | std::min<uint32_t>(frac >> 13, 0x3FFu));
+  const int e = exp - 127 + 15;
+  if (e >= 31) return static_cast<uint16_t>((sign << 15) | 0x7C00u);
+  if (e <= 0) return static_cast<uint16_t>(sign << 15);
+  return static_cast<uint16_t>((sign << 15) | (static_cast<uint32_t>(e) << 10) | (frac >> 13));
+}
+
+float q3_half_to_scale(uint16_t h) {
+  // f16_to_f32, src/lib.rs:1314-1337 (half subnormals normalised).
+  const uint32_t sign = static_cast<uint32_t>(h >> 15) << 31;
+  const int exp = (h >> 10) & 0x1F;
+  uint32_t frac = h & 0x3FFu, bits;
+  if (exp == 0) {
+    if (frac == 0) {
+      bits = sign;
+    } else {
+      int shift = 0;
+      while ((frac & 0x400u) == 0) {
+        frac <<= 1;
+        ++shift;
+      }
+      bits = sign | (static_cast<uint32_t>(127 - 15 + 1 - shift) << 23) | ((frac & 0x3FFu) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7F800000u | (frac << 13);
+  } else {
+    bits = sign | (static_cast<uint32_t>(exp + 127 - 15) << 23) | (frac << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+namespace {
+
+// CENTROIDS_Q3, src/lib.rs:1339: magnitudes of the four levels, in units of the block scale.
+constexpr float kQ3Levels[4] = {0.0955f, 0.3030f, 0.5496f, 0.8849f};
+
+// Index of the level nearest to mag / scale (the first of equally near ones) and its distance.
+inline int q3_nearest(float mag, float scale, float* dist) {
+  int best = 0;
+  float dmin = std::fabs(mag - scale * kQ3Levels[0]);
+  for (int k = 1; k < 4; ++k) {
+    const float dk = std::fabs(mag - scale * kQ3Levels[k]);
+    if (dk < dmin) {
+      dmin = dk;
+      best = k;
+    }
+  }
+  *dist = dmin;
+  return best;
+}
+
+void quantize_q3_block(const float* x, uint8_t* o) {
+  // BlockQ3_LUT::quantize, src/lib.rs:1353-1458: signs apart, magnitudes on four levels times a
+  // per-block scale. Four starting scales (max/level3, max, 2.2 rms, 1.6 rms), each refined by four
+  // rounds of nearest-level assignment and least-squares scale; the scale is rounded to half (the
+  // truncating conversion above) and the start with the smallest squared error on that rounded
+  // scale wins (the first on ties).
+  uint32_t signs = 0;
+  float mag[32], max_abs = 0.0f, sum_sq = 0.0f;
+  for (int i = 0; i < 32; ++i) {
+    if (x[i] < 0.0f) signs |= 1u << i;
+    mag[i] = std::fabs(x[i]);
+    if (mag[i] > max_abs) max_abs = mag[i];
+    sum_sq += mag[i] * mag[i];
+  }
+  std::memset(o, 0, 14);
+  if (max_abs < 1e-8f) return;
+  const float rms = std::sqrt(sum_sq / 32.0f);
+  const float starts[4] = {max_abs / kQ3Levels[3], max_abs, rms * 2.2f, rms * 1.6f};
+  float best_err = 3.40282347e38f;
+  uint16_t best_half = 0;
+  uint8_t best_idx[32] = {};
+  for (float s0 : starts) {
+    float s = std::fmax(s0, 1e-8f);  // f32::max: a NaN operand yields the other one
+    uint8_t idx[32];
+    float unused;
+    for (int round = 0; round < 4; ++round) {
+      float num = 0.0f, den = 0.0f;
+      for (int i = 0; i < 32; ++i) {
+        idx[i] = static_cast<uint8_t>(q3_nearest(mag[i], s, &unused));
+        const float lv = kQ3Levels[idx[i]];
+        num += mag[i] * lv;
+        den += lv * lv;
+      }
+      if (den > 1e-8f) s = num / den;
+    }
+    const uint16_t half = q3_scale_to_half(s);
+    const float sq = q3_half_to_scale(half);
+    float err = 0.0f;
+    for (int i = 0; i < 32; ++i) {
+      idx[i] = static_cast<uint8_t>(q3_nearest(mag[i], sq, &unused));
+      const float diff = mag[i] - sq * kQ3Levels[idx[i]];
+      err += diff * diff;
+    }
+    if (err < best_err) {
+      best_err = err;
+      best_half = half;
+      std::memcpy(best_idx, idx, 32);
+    }
+  }
+  std::memcpy(o, &signs, 4);  // little-endian sign bits
+  for (int b = 0; b < 8; ++b)
+    o[4 + b] = static_cast<uint8_t>((best_idx[4 * b] & 3) | ((best_idx[4 * b + 1] & 3) << 2) |
+                                    ((best_idx[4 * b + 2] & 3) << 4) | ((best_idx[4 * b + 3] & 3) << 6));
+  std::memcpy(o + 12, &best_half, 2);
+}
+
+}  // namespace
+
+void quantize_q3(const float* src, int64_t n, uint8_t* dst) {
+  parallel_for(n / 32, [&](int64_t b0, int64_t b1) {
+    for (int64_t b = b0; b < b1; ++b) quantize_q3_block(src + b * 32, dst + b * 14);
   });
 }
 

@@ -36,6 +36,11 @@ void tensor_layout(const esm_config& c, int dtype, int64_t out_bytes[ESM_NUM_TEN
 
 void quantize_q8(const float* src, int64_t n, uint8_t* dst);
 void quantize_q4(const float* src, int64_t n, uint8_t* dst);
+void quantize_q3(const float* src, int64_t n, uint8_t* dst);  // BlockQ3_LUT, 14 bytes per 32 values
+uint16_t q3_scale_to_half(float v);                            // f32_to_f16 of the reference
+float q3_half_to_scale(uint16_t h);                            // f16_to_f32 of the reference
+// Storage type of tensor `tensor` (EsmWeights order) in a model of type `model_dtype`.
+int matrix_dtype(int model_dtype, int tensor);
 int tokenize(const char* seq, int32_t* out, int32_t cap, int32_t* n_out);
 
 }  // namespace esm

@@ -177,6 +177,40 @@ __global__ void layernorm_kernel(const float* __restrict__ x, int T, int d, cons
   }
 }
 
+// BlockQ3_LUT (14 bytes, byte-aligned): 32 sign bits, 32 two-bit level indices (element e in bits
+// 2 (e % 4) of byte e / 4), the scale as a half in the reference's own encoding (f16_to_f32,
+// src/lib.rs:1314-1337, restated bit for bit). Element e = +-level[idx] * scale, the negative
+// entries being (-level) * scale as the reference's lookup table holds them (src/lib.rs:1461-1501).
+constexpr int kQ3BlockBytes = 14;
+__device__ __forceinline__ float q3_half_to_float(uint32_t h) {
+  const uint32_t sign = (h >> 15) << 31;
+  const int exp = (h >> 10) & 0x1F;
+  uint32_t frac = h & 0x3FFu;
+  if (exp == 0) {
+    if (frac == 0) return __uint_as_float(sign);
+    int shift = 0;
+    while ((frac & 0x400u) == 0) {
+      frac <<= 1;
+      ++shift;
+    }
+    return __uint_as_float(sign | (static_cast<uint32_t>(127 - 15 + 1 - shift) << 23) | ((frac & 0x3FFu) << 13));
+  }
+  if (exp == 31) return __uint_as_float(sign | 0x7F800000u | (frac << 13));
+  return __uint_as_float(sign | (static_cast<uint32_t>(exp + 127 - 15) << 23) | (frac << 13));
+}
+// Elements [8 part, 8 part + 8) of the Q3_LUT block at `blk`.
+__device__ __forceinline__ void q3_part(const uint8_t* blk, int part, float* v) {
+  const float s = q3_half_to_float(static_cast<uint32_t>(blk[12]) | (static_cast<uint32_t>(blk[13]) << 8));
+  const uint32_t sg = blk[part];
+  const uint32_t ix = static_cast<uint32_t>(blk[4 + 2 * part]) | (static_cast<uint32_t>(blk[5 + 2 * part]) << 8);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t k = (ix >> (2 * e)) & 3u;  // CENTROIDS_Q3, src/lib.rs:1339
+    const float lv = k == 0 ? 0.0955f : (k == 1 ? 0.3030f : (k == 2 ? 0.5496f : 0.8849f));
+    v[e] = ((sg >> e) & 1u) ? __fmul_rn(-lv, s) : __fmul_rn(lv, s);
+  }
+}
+
 // One thread per 32-element block: reads the block (fp32 or BlockQ8_0 / BlockQ4_0 bytes) and
 // returns its 32 values as q*d in f32, as BlockQ8_0/BlockQ4_0::dequantize_to do
 // (src/lib.rs:662-667, 1074-1082).
@@ -200,7 +234,7 @@ __device__ __forceinline__ void load_block(int dtype, const void* src, int64_t b
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[4 * i + j] = static_cast<float>(static_cast<int8_t>((q >> (8 * j)) & 0xFF)) * ds;
     }
-  } else {
+  } else if (dtype == 2) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(src) + blk * kQ4BlockBytes);
     const float ds = __uint_as_float(w[0]);
 #pragma unroll
@@ -213,6 +247,9 @@ __device__ __forceinline__ void load_block(int dtype, const void* src, int64_t b
         v[4 * i + j + 16] = static_cast<float>(static_cast<int>(byte >> 4) - 8) * ds;
       }
     }
+  } else {
+#pragma unroll
+    for (int part = 0; part < 4; ++part) q3_part(static_cast<const uint8_t*>(src) + blk * kQ3BlockBytes, part, v + 8 * part);
   }
 }
 
@@ -252,6 +289,8 @@ __device__ __forceinline__ void load_block_part(int dtype, const void* src, int6
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[4 * i + j] = static_cast<float>(static_cast<int8_t>((q >> (8 * j)) & 0xFF)) * ds;
     }
+  } else if (dtype == 3) {
+    q3_part(static_cast<const uint8_t*>(src) + blk * kQ3BlockBytes, part, v);
   } else {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(src) + blk * kQ4BlockBytes);
     const float ds = __uint_as_float(w[0]);
@@ -276,17 +315,19 @@ __global__ void dequant_layer_kernel(LayerSrc src, LayerDst dst, int64_t total_q
     const void* w = src.w[0];
     __half* o = dst.dst[0];
     int64_t base = 0;
+    int dt = src.dtype[0];
 #pragma unroll
     for (int i = 0; i < 5; ++i) {
       if (g >= dst.blk_end[i]) {
         w = src.w[i + 1];
         o = dst.dst[i + 1];
         base = dst.blk_end[i];
+        dt = src.dtype[i + 1];
       }
     }
     const int64_t blk = g - base;
     float v[8];
-    load_block_part(src.dtype, w, blk, part, v);
+    load_block_part(dt, w, blk, part, v);
     __half2 h[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);

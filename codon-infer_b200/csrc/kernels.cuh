@@ -18,7 +18,7 @@ constexpr int kQ4BlockBytes = 20;
 // One layer's weight matrices for the dequantizing conversion to fp16 (dtype = ESM_DTYPE_*):
 // q, k, v, o, fc1, fc2 as fp32 arrays (dtype 0) or block arrays (dtype 1 / 2).
 struct LayerSrc {
-  int dtype;
+  int dtype[6];      // storage type of each matrix (a Q3_LUT model mixes Q4_0 and Q3_LUT)
   const void* w[6];
   int64_t elems[6];  // element count of each matrix
 };

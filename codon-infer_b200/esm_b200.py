@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libesm_b200.so"
 
 ESM_OK, ESM_EINVAL, ESM_EFORMAT, ESM_ECAPACITY, ESM_ECUDA, ESM_ENCCL, ESM_ETIMEOUT, ESM_ENOMEM, ESM_EIO = range(9)
-DTYPE_FP32, DTYPE_Q8_0, DTYPE_Q4_0 = 0, 1, 2
+DTYPE_FP32, DTYPE_Q8_0, DTYPE_Q4_0, DTYPE_Q3_LUT = 0, 1, 2, 3
 ARCH_8M, ARCH_35M, ARCH_150M, ARCH_650M, ARCH_3B = range(5)
 Q8_BLOCK_BYTES, Q4_BLOCK_BYTES = 36, 20
 MASK_ID = 32
@@ -99,6 +99,7 @@ def lib() -> ctypes.CDLL:
             "esm_config_detect_file": [ctypes.c_char_p, vp, vp],
             "esm_quantize_q8": [vp, i64, vp],
             "esm_quantize_q4": [vp, i64, vp],
+            "esm_quantize_q3": [vp, i64, vp],
             "esm_tokenize": [ctypes.c_char_p, vp, i32, vp],
             "esm_ctx_create": [i32, vp],
             "esm_ctx_destroy": [vp],
@@ -155,6 +156,14 @@ def quantize_q4(x) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32).ravel()
     out = np.empty(x.size // 32 * Q4_BLOCK_BYTES, dtype=np.uint8)
     _check(lib().esm_quantize_q4(_p(x), x.size, _p(out)), "esm_quantize_q4")
+    return out
+
+
+def quantize_q3(x) -> np.ndarray:
+    """BlockQ3_LUT blocks (14 bytes each) of a float32 array whose size is a multiple of 32."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(x.size // 32 * 14, dtype=np.uint8)
+    _check(lib().esm_quantize_q3(_p(x), x.size, _p(out)), "esm_quantize_q3")
     return out
 
 
@@ -235,8 +244,13 @@ def quantize_tensors(t: dict, dtype: int) -> dict:
     blocks; for Q8_0 the token embedding is quantized too, for Q4_0 it stays FP32."""
     if dtype == DTYPE_FP32:
         return dict(t)
-    q = quantize_q8 if dtype == DTYPE_Q8_0 else quantize_q4
     out = dict(t)
+    if dtype == DTYPE_Q3_LUT:
+        # EsmWeights::quantize_q3 (src/lib.rs:609-633): Q4_0 attention matrices, Q3_LUT fc1 / fc2.
+        for m in MATRICES:
+            out[m] = quantize_q3(t[m]) if m in ("fc1_w", "fc2_w") else quantize_q4(t[m])
+        return out
+    q = quantize_q8 if dtype == DTYPE_Q8_0 else quantize_q4
     for m in MATRICES:
         out[m] = q(t[m])
     if dtype == DTYPE_Q8_0:

@@ -34,7 +34,7 @@ enum {
 };
 
 /* Weight storage types: CODQ dtype ids, src/lib.rs:874-876. */
-enum { ESM_DTYPE_FP32 = 0, ESM_DTYPE_Q8_0 = 1, ESM_DTYPE_Q4_0 = 2 };
+enum { ESM_DTYPE_FP32 = 0, ESM_DTYPE_Q8_0 = 1, ESM_DTYPE_Q4_0 = 2, ESM_DTYPE_Q3_LUT = 3 };
 
 /* Architecture ids: CODQ arch ids, src/lib.rs:879-883. */
 enum { ESM_ARCH_8M = 0, ESM_ARCH_35M = 1, ESM_ARCH_150M = 2, ESM_ARCH_650M = 3, ESM_ARCH_3B = 4 };
@@ -78,6 +78,11 @@ int esm_config_detect_file(const char* path, esm_config* out, int32_t* dtype);
 int esm_quantize_q8(const float* src, int64_t n, void* dst);
 /* quantize_slice_to_q4 / BlockQ4_0::quantize, src/lib.rs:1054-1088: dst holds n/32 x 20 bytes. */
 int esm_quantize_q4(const float* src, int64_t n, void* dst);
+/* quantize_slice_to_q3_lut / BlockQ3_LUT::quantize, src/lib.rs:1353-1458, 1511-1514: dst holds
+ * n/32 x 14 bytes (32 sign bits, 32 two-bit level indices, the f16 scale of the reference's
+ * truncating conversion). A Q3_LUT model (EsmWeights::quantize_q3, src/lib.rs:609-633) stores fc1
+ * and fc2 this way and its attention matrices as Q4_0. */
+int esm_quantize_q3(const float* src, int64_t n, void* dst);
 /* The same two quantizers on device memory (dtype ESM_DTYPE_Q8_0 or ESM_DTYPE_Q4_0): d_src holds
  * n FP32 values (n % 32 == 0, 16-byte aligned), d_dst receives the n/32 blocks (4-byte aligned),
  * byte-identical to esm_quantize_q8/q4. Enqueued on `stream` (a cudaStream_t; NULL = the legacy

@@ -9,6 +9,9 @@
 //   * weights row-major [out, in], Q-blocks of 32 along `in`       src/lib.rs:2629-2634, 2389-2391
 //   * BlockQ8_0 {f32 d; i8 qs[32]} 36 B, quantize/dequantize        src/lib.rs:640-673
 //   * BlockQ4_0 {f32 d; u8 qs[16]} 20 B, lo nibble=j, hi=j+16, -8   src/lib.rs:1043-1088
+//   * BlockQ3_LUT {u8 signs[4]; u8 idx[8]; u16 f16 scale} 14 B,
+//     AM-LS quantizer, truncating f32<->f16, 4-level LUT decode       src/lib.rs:1291-1514
+//   * Q3_LUT model: Q4_0 attention matrices, Q3_LUT fc1/fc2          src/lib.rs:609-633, 6159-6506
 //   * tiled GEMM: dequantize a weight row to fp32 (q*d), then a
 //     4-token x 16-lane fp32 FMA dot per output                       src/lib.rs:4446-4531, 4672-4756, 4776-4961
 //   * two-pass LayerNorm, eps 1e-5                                   src/lib.rs:2556-2562
@@ -51,6 +54,14 @@ struct BlockQ4 {
 };
 static_assert(sizeof(BlockQ8) == 36, "BlockQ8_0 is 36 bytes");
 static_assert(sizeof(BlockQ4) == 20, "BlockQ4_0 is 20 bytes");
+#pragma pack(push, 1)
+struct BlockQ3 {
+  uint8_t signs[4];    // bit i: element i is negative
+  uint8_t indices[8];  // element i: bits 2 (i % 4) of byte i / 4
+  uint16_t scale;      // f16 in the reference's own encoding
+};
+#pragma pack(pop)
+static_assert(sizeof(BlockQ3) == 14, "BlockQ3_LUT is 14 bytes");
 
 // Rust's f32::round: half away from zero (same as C roundf).
 inline float rust_round(float x) { return std::roundf(x); }
@@ -208,9 +219,151 @@ __attribute__((target("avx2,fma"))) void dot_row_batch_m4(float* out, int out_st
   }
 }
 
-enum { DT_FP32 = 0, DT_Q8 = 1, DT_Q4 = 2 };
+enum { DT_FP32 = 0, DT_Q8 = 1, DT_Q4 = 2, DT_Q3 = 3 };
 
-// matmul_tiled_{fp32,q8,q4}_parallel, src/lib.rs:4803-4827, 4870-4894, 4937-4961:
+// f32_to_f16, src/lib.rs:1291-1312 (exponent rebias, mantissa truncated, no subnormal halves).
+uint16_t ref_f32_to_f16(float val) {
+  uint32_t bits;
+  std::memcpy(&bits, &val, 4);
+  const uint32_t sign = (bits >> 31) & 1;
+  const int32_t exp = static_cast<int32_t>((bits >> 23) & 0xFF);
+  const uint32_t frac = bits & 0x7FFFFF;
+  if (exp == 0) return static_cast<uint16_t>(sign << 15);
+  if (exp == 0xFF) return static_cast<uint16_t>((sign << 15) | 0x7C00 | std::min<uint32_t>(frac >> 13, 0x3FF));
+  const int32_t new_exp = exp - 127 + 15;
+  if (new_exp >= 31) return static_cast<uint16_t>((sign << 15) | 0x7C00);
+  if (new_exp <= 0) return static_cast<uint16_t>(sign << 15);
+  return static_cast<uint16_t>((sign << 15) | (static_cast<uint32_t>(new_exp) << 10) | (frac >> 13));
+}
+
+// f16_to_f32, src/lib.rs:1314-1337.
+float ref_f16_to_f32(uint16_t val) {
+  const uint32_t sign = static_cast<uint32_t>(val >> 15) << 31;
+  const int32_t exp = (val >> 10) & 0x1F;
+  const uint32_t frac = val & 0x3FF;
+  uint32_t bits;
+  if (exp == 0) {
+    if (frac == 0) {
+      bits = sign;
+    } else {
+      uint32_t f = frac;
+      int32_t shift = 0;
+      while ((f & 0x400) == 0) {
+        f <<= 1;
+        shift += 1;
+      }
+      bits = sign | (static_cast<uint32_t>(127 - 15 + 1 - shift) << 23) | ((f & 0x3FF) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7F800000 | (frac << 13);
+  } else {
+    bits = sign | (static_cast<uint32_t>(exp + 127 - 15) << 23) | (frac << 13);
+  }
+  float r;
+  std::memcpy(&r, &bits, 4);
+  return r;
+}
+
+const float kCentroidsQ3[4] = {0.0955f, 0.3030f, 0.5496f, 0.8849f};  // src/lib.rs:1339
+
+// BlockQ3_LUT::quantize, src/lib.rs:1355-1458: multi-start alternating minimization + least squares.
+BlockQ3 quantize_q3_block(const float* src) {
+  uint32_t signs_u32 = 0;
+  float mags[32];
+  float max_abs = 0.0f, sum_sq = 0.0f;
+  for (int i = 0; i < 32; ++i) {
+    const float v = src[i];
+    if (v < 0.0f) signs_u32 |= 1u << i;
+    const float a = std::fabs(v);
+    mags[i] = a;
+    if (a > max_abs) max_abs = a;
+    sum_sq += a * a;
+  }
+  BlockQ3 out;
+  std::memset(&out, 0, sizeof(out));
+  if (max_abs < 1e-8f) return out;
+  const float rms = std::sqrt(sum_sq / 32.0f);
+  const float init_scales[4] = {max_abs / kCentroidsQ3[3], max_abs, rms * 2.2f, rms * 1.6f};
+  float best_err = 3.40282347e38f;  // f32::MAX
+  uint16_t best_scale_f16 = 0;
+  uint8_t best_indices[32] = {};
+  for (float s_init : init_scales) {
+    float s = std::fmax(s_init, 1e-8f);  // f32::max
+    uint8_t idx_arr[32] = {};
+    for (int step = 0; step < 4; ++step) {
+      float num = 0.0f, den = 0.0f;
+      for (int i = 0; i < 32; ++i) {
+        const float mag = mags[i];
+        uint8_t best_k = 0;
+        float min_d = std::fabs(mag - s * kCentroidsQ3[0]);
+        for (int k = 1; k < 4; ++k) {
+          const float dk = std::fabs(mag - s * kCentroidsQ3[k]);
+          if (dk < min_d) {
+            min_d = dk;
+            best_k = static_cast<uint8_t>(k);
+          }
+        }
+        idx_arr[i] = best_k;
+        const float c = kCentroidsQ3[best_k];
+        num += mag * c;
+        den += c * c;
+      }
+      if (den > 1e-8f) s = num / den;
+    }
+    const uint16_t cand_f16 = ref_f32_to_f16(s);
+    const float s_q = ref_f16_to_f32(cand_f16);
+    float err_sq = 0.0f;
+    for (int i = 0; i < 32; ++i) {
+      const float mag = mags[i];
+      uint8_t best_k = 0;
+      float min_d = std::fabs(mag - s_q * kCentroidsQ3[0]);
+      for (int k = 1; k < 4; ++k) {
+        const float dk = std::fabs(mag - s_q * kCentroidsQ3[k]);
+        if (dk < min_d) {
+          min_d = dk;
+          best_k = static_cast<uint8_t>(k);
+        }
+      }
+      idx_arr[i] = best_k;
+      const float diff = mag - s_q * kCentroidsQ3[best_k];
+      err_sq += diff * diff;
+    }
+    if (err_sq < best_err) {
+      best_err = err_sq;
+      best_scale_f16 = cand_f16;
+      std::memcpy(best_indices, idx_arr, 32);
+    }
+  }
+  std::memcpy(out.signs, &signs_u32, 4);
+  for (int byte_idx = 0; byte_idx < 8; ++byte_idx) {
+    out.indices[byte_idx] = static_cast<uint8_t>(
+        (best_indices[byte_idx * 4] & 0x03) | ((best_indices[byte_idx * 4 + 1] & 0x03) << 2) |
+        ((best_indices[byte_idx * 4 + 2] & 0x03) << 4) | ((best_indices[byte_idx * 4 + 3] & 0x03) << 6));
+  }
+  out.scale = best_scale_f16;
+  return out;
+}
+
+// BlockQ3_LUT::dequantize_to, src/lib.rs:1461-1501, per row (unpack_q3_lut_row, 4759-4764).
+void dequant_q3_row(const BlockQ3* blocks, int nblocks, float* dst) {
+  for (int b = 0; b < nblocks; ++b) {
+    const float s = ref_f16_to_f32(blocks[b].scale);
+    float lut[8];
+    for (int k = 0; k < 4; ++k) {
+      lut[k] = kCentroidsQ3[k] * s;
+      lut[4 + k] = -kCentroidsQ3[k] * s;
+    }
+    uint32_t signs;
+    std::memcpy(&signs, blocks[b].signs, 4);
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t idx = (blocks[b].indices[i / 4] >> (2 * (i % 4))) & 0x03;
+      const uint32_t sign = (signs >> i) & 1;
+      dst[b * 32 + i] = lut[(sign << 2) | idx];
+    }
+  }
+}
+
+// matmul_tiled_{fp32,q8,q4,q3}_parallel, src/lib.rs:4803-4827, 4870-4894, 4937-4961, 4963-5031:
 // out[p, i] = sum_k W[i, k] x[p, k] + bias[i]; weight rows are dequantized to fp32 first.
 void tiled_gemm(int dtype, float* out, const float* x, const void* w, const float* bias, int in_dim,
                 int out_dim, int seq_len, int n_threads) {
@@ -225,8 +378,11 @@ void tiled_gemm(int dtype, float* out, const float* x, const void* w, const floa
       } else if (dtype == DT_Q8) {
         dequant_q8_row(static_cast<const BlockQ8*>(w) + static_cast<size_t>(i) * bpr, bpr, wbuf.data());
         wrow = wbuf.data();
-      } else {
+      } else if (dtype == DT_Q4) {
         dequant_q4_row(static_cast<const BlockQ4*>(w) + static_cast<size_t>(i) * bpr, bpr, wbuf.data());
+        wrow = wbuf.data();
+      } else {
+        dequant_q3_row(static_cast<const BlockQ3*>(w) + static_cast<size_t>(i) * bpr, bpr, wbuf.data());
         wrow = wbuf.data();
       }
       dot_row_batch_m4(out, out_dim, i, x, wrow, bias[i], in_dim, seq_len);
@@ -295,6 +451,7 @@ struct Weights {
 size_t weight_elems_bytes(int dtype, size_t elems) {
   if (dtype == DT_FP32) return elems * 4;
   if (dtype == DT_Q8) return elems / 32 * sizeof(BlockQ8);
+  if (dtype == DT_Q3) return elems / 32 * sizeof(BlockQ3);
   return elems / 32 * sizeof(BlockQ4);
 }
 
@@ -318,6 +475,13 @@ void orc_dequantize_q8(const void* src, int64_t n, float* dst) {
 }
 void orc_dequantize_q4(const void* src, int64_t n, float* dst) {
   dequant_q4_row(static_cast<const BlockQ4*>(src), static_cast<int>(n / 32), dst);
+}
+void orc_quantize_q3(const float* src, int64_t n, void* dst) {
+  BlockQ3* out = static_cast<BlockQ3*>(dst);
+  for (int64_t b = 0; b < n / 32; ++b) out[b] = quantize_q3_block(src + b * 32);
+}
+void orc_dequantize_q3(const void* src, int64_t n, float* dst) {
+  dequant_q3_row(static_cast<const BlockQ3*>(src), static_cast<int>(n / 32), dst);
 }
 
 // --- single kernels, exposed for the known-answer tests ----------------------------------------
@@ -458,17 +622,21 @@ int orc_forward(const int* cfg5, int dtype, const void* const* tensors, int64_t 
   }
   std::vector<float> att_rows(static_cast<size_t>(L) * L);
 
-  const size_t mat_b = weight_elems_bytes(dtype, static_cast<size_t>(d) * d);
-  const size_t fc1_b = weight_elems_bytes(dtype, static_cast<size_t>(d) * F);
-  const size_t fc2_b = weight_elems_bytes(dtype, static_cast<size_t>(F) * d);
+  // forward_bidirectional_q3_ext (src/lib.rs:6159-6506) runs the attention projections as Q4_0
+  // and fc1 / fc2 as Q3_LUT; the other model types use one matrix type throughout.
+  const int dt_att = dtype == DT_Q3 ? DT_Q4 : dtype;
+  const int dt_fc = dtype;
+  const size_t mat_b = weight_elems_bytes(dt_att, static_cast<size_t>(d) * d);
+  const size_t fc1_b = weight_elems_bytes(dt_fc, static_cast<size_t>(d) * F);
+  const size_t fc2_b = weight_elems_bytes(dt_fc, static_cast<size_t>(F) * d);
 
   for (int l = 0; l < cfg.n_layers; ++l) {
     const float* ln1w = W.ln1_w + static_cast<size_t>(l) * d;
     const float* ln1b = W.ln1_b + static_cast<size_t>(l) * d;
     for (int p = 0; p < L; ++p) layer_norm(&xb[static_cast<size_t>(p) * d], &x[static_cast<size_t>(p) * d], ln1w, ln1b, d);
-    tiled_gemm(dtype, q.data(), xb.data(), byte_offset(W.wq, l * mat_b), W.bq + static_cast<size_t>(l) * d, d, d, L, n_threads);
-    tiled_gemm(dtype, k.data(), xb.data(), byte_offset(W.wk, l * mat_b), W.bk + static_cast<size_t>(l) * d, d, d, L, n_threads);
-    tiled_gemm(dtype, v.data(), xb.data(), byte_offset(W.wv, l * mat_b), W.bv + static_cast<size_t>(l) * d, d, d, L, n_threads);
+    tiled_gemm(dt_att, q.data(), xb.data(), byte_offset(W.wq, l * mat_b), W.bq + static_cast<size_t>(l) * d, d, d, L, n_threads);
+    tiled_gemm(dt_att, k.data(), xb.data(), byte_offset(W.wk, l * mat_b), W.bk + static_cast<size_t>(l) * d, d, d, L, n_threads);
+    tiled_gemm(dt_att, v.data(), xb.data(), byte_offset(W.wv, l * mat_b), W.bv + static_cast<size_t>(l) * d, d, d, L, n_threads);
 
     // apply_rope, src/lib.rs:3533-3552.
     for (int p = 0; p < L; ++p) {
@@ -516,15 +684,15 @@ int orc_forward(const int* cfg5, int dtype, const void* const* tensors, int64_t 
       }
     }
 
-    tiled_gemm(dtype, xb.data(), out_att.data(), byte_offset(W.wo, l * mat_b), W.bo + static_cast<size_t>(l) * d, d, d, L, n_threads);
+    tiled_gemm(dt_att, xb.data(), out_att.data(), byte_offset(W.wo, l * mat_b), W.bo + static_cast<size_t>(l) * d, d, d, L, n_threads);
     for (size_t i = 0; i < static_cast<size_t>(L) * d; ++i) x[i] += xb[i];
 
     const float* ln2w = W.ln2_w + static_cast<size_t>(l) * d;
     const float* ln2b = W.ln2_b + static_cast<size_t>(l) * d;
     for (int p = 0; p < L; ++p) layer_norm(&xb[static_cast<size_t>(p) * d], &x[static_cast<size_t>(p) * d], ln2w, ln2b, d);
-    tiled_gemm(dtype, hb.data(), xb.data(), byte_offset(W.fc1_w, l * fc1_b), W.fc1_b + static_cast<size_t>(l) * F, d, F, L, n_threads);
+    tiled_gemm(dt_fc, hb.data(), xb.data(), byte_offset(W.fc1_w, l * fc1_b), W.fc1_b + static_cast<size_t>(l) * F, d, F, L, n_threads);
     for (size_t i = 0; i < static_cast<size_t>(L) * F; ++i) hb2[i] = gelu(hb[i]);
-    tiled_gemm(dtype, xb.data(), hb2.data(), byte_offset(W.fc2_w, l * fc2_b), W.fc2_b + static_cast<size_t>(l) * d, F, d, L, n_threads);
+    tiled_gemm(dt_fc, xb.data(), hb2.data(), byte_offset(W.fc2_w, l * fc2_b), W.fc2_b + static_cast<size_t>(l) * d, F, d, L, n_threads);
     for (size_t i = 0; i < static_cast<size_t>(L) * d; ++i) x[i] += xb[i];
     if (on_layer) on_layer(l, x.data(), user);
   }

@@ -19,7 +19,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libesm_oracle.so"
 
-DT_FP32, DT_Q8, DT_Q4 = 0, 1, 2
+DT_FP32, DT_Q8, DT_Q4, DT_Q3 = 0, 1, 2, 3
 Q8_BLOCK_BYTES = 36  # BlockQ8_0 {f32 d; i8 qs[32]}, src/lib.rs:640-645
 Q4_BLOCK_BYTES = 20  # BlockQ4_0 {f32 d; u8 qs[16]}, src/lib.rs:1043-1051
 
@@ -50,6 +50,8 @@ def lib() -> ctypes.CDLL:
         L.orc_quantize_q4.argtypes = [vp, i64, vp]
         L.orc_dequantize_q8.argtypes = [vp, i64, vp]
         L.orc_dequantize_q4.argtypes = [vp, i64, vp]
+        L.orc_quantize_q3.argtypes = [vp, i64, vp]
+        L.orc_dequantize_q3.argtypes = [vp, i64, vp]
         L.orc_tiled_gemm.argtypes = [ctypes.c_int, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_layer_norm.argtypes = [vp, vp, vp, vp, ctypes.c_int]
         L.orc_gelu.argtypes = [ctypes.c_float]
@@ -109,6 +111,23 @@ def dequantize_q4(blocks: np.ndarray) -> np.ndarray:
     return out
 
 
+def quantize_q3(x) -> np.ndarray:
+    """BlockQ3_LUT blocks (raw bytes, 14 per block) of a float32 array whose size is a multiple of 32."""
+    x = _f32(x).ravel()
+    assert x.size % 32 == 0
+    out = np.empty(x.size // 32 * 14, dtype=np.uint8)
+    lib().orc_quantize_q3(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def dequantize_q3(blocks: np.ndarray) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    n = blocks.size // 14 * 32
+    out = np.empty(n, dtype=np.float32)
+    lib().orc_dequantize_q3(_ptr(blocks), n, _ptr(out))
+    return out
+
+
 def tiled_gemm(dtype: int, x: np.ndarray, w: np.ndarray, bias: np.ndarray, in_dim: int, out_dim: int,
                n_threads: int = 1) -> np.ndarray:
     """matmul_tiled_{fp32,q8,q4}_parallel: [L, in] x W[out, in]^T + b -> [L, out]."""
@@ -159,7 +178,7 @@ def accumulate_head_apc(head_att, contact_logits: np.ndarray, seq_len: int, n_re
 
 def forward(cfg, dtype: int, tensors: dict, tokens, n_threads: int | None = None,
             contact_w=None, contact_b: float = 0.0, want_hidden: bool = False, on_layer=None):
-    """One sequence through the reference forward (FP32 / Q8_0 / Q4_0 by ``dtype``).
+    """One sequence through the reference forward (FP32 / Q8_0 / Q4_0 / Q3_LUT by ``dtype``).
 
     ``cfg`` has dim, hidden_dim, n_layers, n_heads, vocab_size; ``tensors`` maps TENSOR_NAMES to
     numpy arrays (float32, or uint8 block bytes for quantized matrices). Returns a dict with

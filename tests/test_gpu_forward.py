@@ -108,6 +108,36 @@ def test_650m_q4(esm, orc):
     compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out)
 
 
+def test_q3_lut_models(esm, orc, tmp_path):
+    # Q3_LUT models (EsmWeights::quantize_q3, forward_bidirectional_q3, src/lib.rs:609-633,
+    # 6159-6506): Q4_0 attention matrices and Q3_LUT fc1 / fc2, decoded per layer on the GPU. A
+    # 650M-shape model with contacts against the oracle, and the 8M preset through a CODQ file.
+    base = esm.esm2_650m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    m, t, cw = build(esm, cfg, esm.DTYPE_Q3_LUT, seed=8)
+    lens = [33, 130, 257]
+    m.reserve(sum(lens), len(lens), 257, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=9)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_Q3_LUT, t, seqs, out, cw)
+    m.close()
+
+    cfg8 = esm.esm2_8m()
+    t8 = esm.quantize_tensors(esm.synth_fp32_tensors(cfg8, seed=10), esm.DTYPE_Q3_LUT)
+    path = tmp_path / "esm2_8m.codq"
+    esm.write_codq(str(path), cfg8, esm.DTYPE_Q3_LUT, t8)
+    seqs8 = esm.random_sequences(2, [40, 90], seed=11)
+    outs = []
+    for load in (lambda mm: mm.load_tensors(cfg8, esm.DTYPE_Q3_LUT, t8), lambda mm: mm.load_file(str(path))):
+        mm = esm.Model(0)
+        load(mm)
+        mm.reserve(130, 2, 90)
+        outs.append(mm.forward(seqs8)["logits"])
+        mm.close()
+    np.testing.assert_array_equal(outs[0], outs[1])
+    compare(orc, cfg8, esm.DTYPE_Q3_LUT, t8, seqs8, {"logits": outs[0]})
+
+
 def test_3b_shape_q8_contacts_beyond_1024(esm, orc):
     # Config 5 shapes (d 2560, 40 heads x 64, FFN 10240, Q8_0) with two layers, one sequence longer
     # than the reference's 1024-entry APC buffer allows, contacts on.

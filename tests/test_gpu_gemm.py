@@ -1,5 +1,5 @@
 """GPU parity of the tcgen05 projection GEMM through the C ABI (esm_matmul_tiled) against the
-oracle's restatement of matmul_tiled_{fp32,q8,q4}_parallel.
+oracle's restatement of matmul_tiled_{fp32,q8,q4,q3}_parallel.
 
 Tolerance: the tensor cores see fp16 operands (x and the dequantized weight q*d each rounded once,
 relative error <= 2^-11) and accumulate in fp32, so element (p, i) may differ from the fp32
@@ -33,9 +33,12 @@ def _check(model, orc, dt, x, w_f32, bias, in_dim, out_dim):
     elif dt == 1:
         wq = orc.quantize_q8(w_f32)
         deq = orc.dequantize_q8(wq)
-    else:
+    elif dt == 2:
         wq = orc.quantize_q4(w_f32)
         deq = orc.dequantize_q4(wq)
+    else:
+        wq = orc.quantize_q3(w_f32)
+        deq = orc.dequantize_q3(wq)
     got = model.matmul_tiled(dt, x, wq, bias, in_dim, out_dim)
     ref = orc.tiled_gemm(dt, x, wq, bias if bias is not None else np.zeros(out_dim, np.float32), in_dim, out_dim,
                          n_threads=8)
@@ -45,7 +48,7 @@ def _check(model, orc, dt, x, w_f32, bias, in_dim, out_dim):
     assert (err <= bound).all(), f"max err {err.max():.3e}, worst excess {(err - bound).max():.3e}"
 
 
-@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("dt", [0, 1, 2, 3])
 @pytest.mark.parametrize("seq_len", [7, 12])
 def test_reference_tiled_vs_gemv_case(model, orc, dt, seq_len):
     # The reference's tiled-GEMM test inputs (src/lib.rs:8473-8515): (320 -> 64), seq 7 and 12.
@@ -56,7 +59,7 @@ def test_reference_tiled_vs_gemv_case(model, orc, dt, seq_len):
     _check(model, orc, dt, x, w, b, in_dim, out_dim)
 
 
-@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("dt", [0, 1, 2, 3])
 @pytest.mark.parametrize("shape", [
     (1280, 5120, 300),   # 650M fc1
     (5120, 1280, 257),   # 650M fc2, ragged M
