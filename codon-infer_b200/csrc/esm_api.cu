@@ -226,11 +226,16 @@ int build_weight_maps(esm_ctx* c) {
   return ok ? ESM_OK : fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for a weight matrix");
 }
 
-// Tensors of a Q8_0 / Q4_0 model that are stored as blocks (EsmWeights::quantize_q8 / quantize_q4,
-// src/lib.rs:559-607): the six matrices of every layer, and for Q8_0 the token embedding.
+// Tensors of a Q8_0 / Q4_0 / Q3_LUT model quantized on the device while loading
+// (EsmWeights::quantize_q8 / quantize_q4 / quantize_q3, src/lib.rs:559-633): the six matrices of
+// every layer, for Q8_0 also the token embedding; for Q3_LUT only the four Q4_0 attention
+// matrices (its Q3_LUT fc1 / fc2 are quantized on the host, see load_fp32_as).
 uint32_t quantized_tensors(int dtype) {
-  const uint32_t mats = (1u << 3) | (1u << 5) | (1u << 7) | (1u << 9) | (1u << 13) | (1u << 15);
-  return dtype == ESM_DTYPE_Q8_0 ? (mats | 1u) : (dtype == ESM_DTYPE_Q4_0 ? mats : 0u);
+  const uint32_t att = (1u << 3) | (1u << 5) | (1u << 7) | (1u << 9), fc = (1u << 13) | (1u << 15);
+  if (dtype == ESM_DTYPE_Q8_0) return att | fc | 1u;
+  if (dtype == ESM_DTYPE_Q4_0) return att | fc;
+  if (dtype == ESM_DTYPE_Q3_LUT) return att;
+  return 0u;
 }
 
 // Uploads a weight set. Tensor i with bit i of `quantize_mask` set is given as FP32 host data
@@ -243,11 +248,11 @@ int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* con
   if (!shape_supported(cfg, &why)) return fail(c, ESM_EINVAL, "unsupported model shape: " + why);
   int64_t expect[ESM_NUM_TENSORS];
   esm::tensor_layout(cfg, dtype, expect);
-  const int64_t block_bytes = dtype == ESM_DTYPE_Q8_0 ? 36 : 20;
   for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
     if (tensors[i] == nullptr && !(i == 19 && sizes[i] == 0))
       return fail(c, ESM_EINVAL, "tensor " + std::to_string(i) + " is null");
     const bool q = (quantize_mask >> i) & 1u;
+    const int64_t block_bytes = esm::matrix_dtype(dtype, i) == ESM_DTYPE_Q8_0 ? 36 : 20;
     const int64_t want = q ? expect[i] / block_bytes * 128 : expect[i];  // 32 floats per block
     if (i < 19 && static_cast<int64_t>(sizes[i]) != want)
       return fail(c, ESM_EFORMAT, "tensor " + std::to_string(i) + " has " + std::to_string(sizes[i]) +
@@ -285,7 +290,9 @@ int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* con
       rc = dev_alloc(c, tmp, &f, sizes[i] / 4);
       if (rc) return rc;
       cudaError_t e = cudaMemcpyAsync(f, tensors[i], sizes[i], cudaMemcpyHostToDevice, c->stream);
-      if (e == cudaSuccess) e = esm::launch_quantize(dtype, f, static_cast<int64_t>(sizes[i] / 128), p, c->stream);
+      if (e == cudaSuccess)
+        e = esm::launch_quantize(i == 0 ? dtype : esm::matrix_dtype(dtype, i), f, static_cast<int64_t>(sizes[i] / 128),
+                                 p, c->stream);
       if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
       free_list(tmp);
       if (e != cudaSuccess) return fail(c, ESM_ECUDA, std::string("device quantization: ") + cudaGetErrorString(e));
@@ -923,6 +930,30 @@ int esm_load_host(esm_ctx* c, const esm_config* cfg, int32_t dtype, const void* 
 
 namespace {
 
+// An FP32 weight set (host memory) loaded as a `dtype` model: the device quantizes what it can
+// (Q8_0 / Q4_0 blocks); a Q3_LUT model's fc1 / fc2 go through the host quantizer first
+// (BlockQ3_LUT's iterative fit is a load-time format conversion with no device version here).
+int load_fp32_as(esm_ctx* c, const esm_config& cfg, int dtype, const void* const* tensors, const size_t* sizes) {
+  if (dtype != ESM_DTYPE_Q3_LUT) return load_host_impl(c, cfg, dtype, tensors, sizes, quantized_tensors(dtype));
+  const void* ptr[ESM_NUM_TENSORS];
+  size_t sz[ESM_NUM_TENSORS];
+  std::vector<uint8_t> q3[2];
+  for (int i = 0; i < ESM_NUM_TENSORS; ++i) {
+    ptr[i] = tensors[i];
+    sz[i] = sizes[i];
+  }
+  for (int k = 0; k < 2; ++k) {
+    const int i = k ? 15 : 13;
+    if (!tensors[i] || sizes[i] % 128) return fail(c, ESM_EFORMAT, "tensor " + std::to_string(i) + " is not FP32 blocks");
+    const int64_t n = static_cast<int64_t>(sizes[i] / 4);
+    q3[k].resize(static_cast<size_t>(n / 32 * 14));
+    esm::quantize_q3(static_cast<const float*>(tensors[i]), n, q3[k].data());
+    ptr[i] = q3[k].data();
+    sz[i] = q3[k].size();
+  }
+  return load_host_impl(c, cfg, dtype, ptr, sz, quantized_tensors(dtype));
+}
+
 // Reads a CODQ or header-less weight file into host memory and splits it into the 20 tensors
 // (EsmWeights{,Q8,Q4}::from_file, src/lib.rs:310-547, 744-830, 1156-1242).
 struct WeightFile {
@@ -1079,24 +1110,33 @@ int esm_load_file(esm_ctx* c, const char* path, const esm_config* cfg_in) {
 
 int esm_load_file_quantized(esm_ctx* c, const char* path, const esm_config* cfg_in, int32_t dtype) {
   if (!c || !path) return fail(c, ESM_EINVAL, "null argument");
-  if (dtype != ESM_DTYPE_Q8_0 && dtype != ESM_DTYPE_Q4_0) return fail(c, ESM_EINVAL, "dtype must be Q8_0 or Q4_0");
+  if (dtype < ESM_DTYPE_Q8_0 || dtype > ESM_DTYPE_Q3_LUT) return fail(c, ESM_EINVAL, "dtype must be Q8_0, Q4_0 or Q3_LUT");
   std::lock_guard<std::mutex> lk(c->mu);
   WeightFile wf;
   const int rc = read_weight_file(c, path, cfg_in, wf);
   if (rc) return rc;
-  // As in load_model_weights, the requested type applies to FP32 files; a Q8_0 / Q4_0 file loads
-  // as it is stored.
+  // As in load_model_weights, the requested type applies to FP32 files; a quantized file loads as
+  // it is stored.
   if (wf.dtype != ESM_DTYPE_FP32) return load_host_impl(c, wf.cfg, wf.dtype, wf.ptr, wf.sizes);
-  return load_host_impl(c, wf.cfg, dtype, wf.ptr, wf.sizes, quantized_tensors(dtype));
+  return load_fp32_as(c, wf.cfg, dtype, wf.ptr, wf.sizes);
 }
 
 int esm_load_host_quantized(esm_ctx* c, const esm_config* cfg, int32_t dtype, const void* const* tensors,
                             const size_t* sizes) {
   if (!c || !cfg || !tensors || !sizes) return fail(c, ESM_EINVAL, "null argument");
-  if (dtype != ESM_DTYPE_Q8_0 && dtype != ESM_DTYPE_Q4_0) return fail(c, ESM_EINVAL, "dtype must be Q8_0 or Q4_0");
+  if (dtype < ESM_DTYPE_Q8_0 || dtype > ESM_DTYPE_Q3_LUT) return fail(c, ESM_EINVAL, "dtype must be Q8_0, Q4_0 or Q3_LUT");
   std::lock_guard<std::mutex> lk(c->mu);
-  return load_host_impl(c, *cfg, dtype, tensors, sizes, quantized_tensors(dtype));
+  return load_fp32_as(c, *cfg, dtype, tensors, sizes);
 }
+
+namespace {
+
+// The ranking of esm_contact_top_pairs on a device map; the caller holds the context lock.
+int contact_rank_locked(esm_ctx* c, const float* d_map, int32_t n, const char* seq, int32_t min_separation,
+                        int32_t max_k, float top_l_factor, int32_t* pos1, int32_t* pos2, float* score,
+                        int32_t* n_out, float* cys_enrichment);
+
+}  // namespace
 
 int esm_contact_top_pairs(esm_ctx* c, const float* d_map, int32_t n, const char* seq, int32_t min_separation,
                           int32_t max_k, float top_l_factor, int32_t* pos1, int32_t* pos2, float* score,
@@ -1107,6 +1147,50 @@ int esm_contact_top_pairs(esm_ctx* c, const float* d_map, int32_t n, const char*
   if (n < 4) return fail(c, ESM_EINVAL, "Sequence too short for contact prediction");
   if (min_separation < 0) return fail(c, ESM_EINVAL, "min_separation must be >= 0");
   std::lock_guard<std::mutex> lk(c->mu);
+  return contact_rank_locked(c, d_map, n, seq, min_separation, max_k, top_l_factor, pos1, pos2, score, n_out,
+                             cys_enrichment);
+}
+
+int esm_contacts_pipeline(esm_ctx* c, const char* seq, int32_t min_separation, int32_t max_k, float top_l_factor,
+                          float* logits, float* contact_probs, int32_t* pos1, int32_t* pos2, float* score,
+                          int32_t* n_out, float* cys_enrichment) {
+  if (!c || !seq || !pos1 || !pos2 || !score || !n_out || !cys_enrichment) return fail(c, ESM_EINVAL, "null argument");
+  const int32_t n = static_cast<int32_t>(std::strlen(seq));
+  if (n < 4) return fail(c, ESM_EINVAL, "Sequence too short for contact prediction");
+  if (min_separation < 0) return fail(c, ESM_EINVAL, "min_separation must be >= 0");
+  std::lock_guard<std::mutex> lk(c->mu);
+  // Tokenizer::encode, then forward_bidirectional* with compute_contacts (src/pipeline.rs:423-445).
+  std::vector<int32_t> toks(static_cast<size_t>(n) + 2);
+  int32_t L = 0;
+  if (esm::tokenize(seq, toks.data(), static_cast<int32_t>(toks.size()), &L) != ESM_OK)
+    return fail(c, ESM_EINVAL, "tokenizer capacity");
+  const int32_t cu[2] = {0, L};
+  int rc = validate_call(c, cu, 1, true);
+  if (rc) return rc;
+  if (!c->has_ch) return fail(c, ESM_EINVAL, "the contact head is not set (esm_set_contact_head)");
+  ESM_CUDA(cudaSetDevice(c->device));
+  cudaStream_t s = c->stream;
+  rc = upload_plan(c, cu, 1, true, s);
+  if (rc) return rc;
+  ESM_CUDA(cudaMemcpyAsync(c->tokens, toks.data(), static_cast<size_t>(L) * 4, cudaMemcpyHostToDevice, s));
+  rc = forward_impl(c, c->tokens, cu, 1, c->logits, nullptr, c->cmap, nullptr, s);
+  if (rc) return rc;
+  if (logits)
+    ESM_CUDA(cudaMemcpyAsync(logits, c->logits, static_cast<size_t>(L) * c->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, s));
+  if (contact_probs)
+    ESM_CUDA(cudaMemcpyAsync(contact_probs, c->cmap, static_cast<size_t>(n) * n * 4, cudaMemcpyDeviceToHost, s));
+  rc = contact_rank_locked(c, c->cmap, n, seq, min_separation, max_k, top_l_factor, pos1, pos2, score, n_out,
+                           cys_enrichment);
+  if (rc) return rc;
+  ESM_CUDA(cudaStreamSynchronize(s));
+  return check_device_word(c);
+}
+
+namespace {
+
+int contact_rank_locked(esm_ctx* c, const float* d_map, int32_t n, const char* seq, int32_t min_separation,
+                        int32_t max_k, float top_l_factor, int32_t* pos1, int32_t* pos2, float* score,
+                        int32_t* n_out, float* cys_enrichment) {
   // Candidate and Cys-Cys pair counts (src/pipeline.rs:454-477).
   int64_t total = 0;
   for (int64_t i = 0; i < n; ++i) total += std::max<int64_t>(0, n - (i + min_separation));
@@ -1160,6 +1244,8 @@ int esm_contact_top_pairs(esm_ctx* c, const float* d_map, int32_t n, const char*
   *cys_enrichment = bg_density > 0.0f ? top_density / bg_density : 1.0f;
   return ESM_OK;
 }
+
+}  // namespace
 
 int esm_quantize_device(int32_t dtype, const float* d_src, int64_t n, void* d_dst, void* stream) {
   if (!d_src || !d_dst || n < 0 || n % 32) return ESM_EINVAL;

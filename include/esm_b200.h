@@ -108,6 +108,16 @@ int esm_contact_top_pairs(esm_ctx* ctx, const float* d_map, int32_t n, const cha
                           int32_t max_k, float top_l_factor, int32_t* pos1, int32_t* pos2, float* score,
                           int32_t* n_out, float* cys_enrichment);
 
+/* compute_pipeline_contacts_parallel (src/pipeline.rs:410-512) for one sequence in one call: seq is
+ * the residue string (n >= 4 letters, tokenized as Tokenizer::encode); the forward with contacts
+ * (contact head set, workspace reserved for n + 2 tokens with contacts) and the ranking of
+ * esm_contact_top_pairs run on the GPU, so the map crosses to the host only when contact_probs
+ * ([n, n], host) is given; logits ([n + 2, vocab], host) is optional too. Outputs as in
+ * esm_contact_top_pairs. */
+int esm_contacts_pipeline(esm_ctx* ctx, const char* seq, int32_t min_separation, int32_t max_k, float top_l_factor,
+                          float* logits, float* contact_probs, int32_t* pos1, int32_t* pos2, float* score,
+                          int32_t* n_out, float* cys_enrichment);
+
 /* ---- context ------------------------------------------------------------------------------ */
 
 int esm_ctx_create(int32_t device, esm_ctx** out);
@@ -122,15 +132,17 @@ int esm_load_file(esm_ctx* ctx, const char* path, const esm_config* cfg);
 int esm_load_host(esm_ctx* ctx, const esm_config* cfg, int32_t dtype, const void* const* tensors,
                   const size_t* sizes);
 
-/* EsmWeights::quantize_q8 / quantize_q4 (src/lib.rs:559-607) done on the device while uploading:
- * tensors / sizes are an FP32 weight set (the ESM_DTYPE_FP32 layout); the six matrices of every
- * layer, and for Q8_0 the token embedding, are quantized on the GPU into a `dtype` (Q8_0 or Q4_0)
- * model, block for block identical to the host quantizers. */
+/* EsmWeights::quantize_q8 / quantize_q4 / quantize_q3 (src/lib.rs:559-633) done while uploading:
+ * tensors / sizes are an FP32 weight set (the ESM_DTYPE_FP32 layout). For Q8_0 / Q4_0 the six
+ * matrices of every layer (and for Q8_0 the token embedding) are quantized on the GPU; for Q3_LUT
+ * the four attention matrices are quantized to Q4_0 on the GPU and fc1 / fc2 to Q3_LUT on the host.
+ * Block for block identical to the host quantizers. */
 int esm_load_host_quantized(esm_ctx* ctx, const esm_config* cfg, int32_t dtype, const void* const* tensors,
                             const size_t* sizes);
 
-/* load_model_weights with QuantizationMode::Q8_0 / Q4_0 (src/main.rs:137-244): an FP32 weight
- * file is quantized on the device while loading; a Q8_0 / Q4_0 file loads as it is stored. */
+/* load_model_weights with QuantizationMode::Q8_0 / Q4_0 / Q3_LUT (src/main.rs:137-244): an FP32
+ * weight file is quantized while loading (as esm_load_host_quantized); a quantized file loads as it
+ * is stored. */
 int esm_load_file_quantized(esm_ctx* ctx, const char* path, const esm_config* cfg, int32_t dtype);
 
 /* Contact regression head (EsmConfig::contact_head_weights, src/lib.rs:154-177): w has

@@ -285,6 +285,66 @@ static void run_misuse(const std::string& q4) {
   CHECK(truncated);
 }
 
+// The pipelines on an FP32 file quantized to Q4_0 while loading (load_model_weights with
+// QuantizationMode::Q4_0): both mutational-scan modes and the contacts pipeline. Their outputs go
+// to `out` for the Python side to compare with the oracle; the row bookkeeping is checked here.
+static void run_pipelines(const std::string& f32, const std::string& seq, const std::string& out) {
+  LoadedWeights lw = load_model_weights(f32, QuantizationMode::Q4_0);
+  CHECK(lw.mode == QuantizationMode::Q4_0);
+  const EsmConfig& cfg = lw.config;
+  DeviceWeights& w = *lw.weights;
+  std::vector<float> head(cfg.n_layers * cfg.n_heads);
+  for (size_t i = 0; i < head.size(); ++i) head[i] = (i % 3 == 0) ? 0.0f : 0.05f * std::sin(0.7f * i);
+  w.set_contact_head(head, -0.5f);
+  const FastaRecord rec{"test", "test protein", seq};
+  const DmsPipelineResult mm = run_pipeline_dms_with_mode(rec, 0, 0, cfg, w, 8, DmsScoringMode::MaskedMarginal);
+  const DmsPipelineResult wt = run_pipeline_dms_with_mode(rec, 16, 5, cfg, w, 8, DmsScoringMode::WildtypeMarginal);
+  const size_t n = seq.size();
+  for (const DmsPipelineResult* r : {&mm, &wt}) {
+    CHECK(r->rows.size() == n);
+    size_t catalytic = 0;
+    for (size_t p = 0; p < n; ++p) {
+      const DmsPositionRow& row = r->rows[p];
+      CHECK(row.pos == p + 1 && row.wt == seq[p]);
+      float sum = 0.0f;
+      for (float d : row.deltas) sum += (d != 0.0f) ? d : 0.0f;
+      CHECK(row.mean_delta_logp == sum / 19.0f);
+      catalytic += row.mean_delta_logp <= -3.8f;
+    }
+    CHECK(r->catalytic_sites_detected == catalytic);
+    CHECK(r->muts_per_sec > 0.0);
+  }
+  const ContactsPipelineResult cp = compute_pipeline_contacts_parallel(rec, 6, 1.0f, std::nullopt, cfg, w, 8);
+  CHECK(cp.sequence_length == n && cp.contact_probs.size() == n * n);
+  for (const ContactPair& c : cp.top_contacts) CHECK(c.pos2 >= c.pos1 + 6 && c.res1 == seq[c.pos1]);
+  // Q3_LUT blocks through the C++ types: a block decodes to the reference's LUT values.
+  std::vector<float> src(64);
+  for (size_t i = 0; i < src.size(); ++i) src[i] = std::sin(0.37f * static_cast<float>(i));
+  const std::vector<BlockQ3_LUT> q3 = quantize_slice_to_q3_lut(src);
+  CHECK(q3.size() == 2);
+  float dq[64];
+  q3[0].dequantize_to(dq);
+  q3[1].dequantize_to(dq + 32);
+  for (int i = 0; i < 64; ++i) CHECK(std::isfinite(dq[i]) && (src[i] == 0.0f || (dq[i] < 0.0f) == (src[i] < 0.0f)));
+
+  std::ofstream f(out, std::ios::binary);
+  const int32_t hdr[2] = {static_cast<int32_t>(n), static_cast<int32_t>(cp.top_contacts.size())};
+  f.write(reinterpret_cast<const char*>(hdr), 8);
+  for (const DmsPipelineResult* r : {&mm, &wt}) {
+    for (const DmsPositionRow& row : r->rows) f.write(reinterpret_cast<const char*>(row.deltas.data()), 80);
+    for (const DmsPositionRow& row : r->rows) f.write(reinterpret_cast<const char*>(&row.entropy), 4);
+  }
+  for (const ContactPair& c : cp.top_contacts) {
+    const int32_t ij[2] = {static_cast<int32_t>(c.pos1), static_cast<int32_t>(c.pos2)};
+    f.write(reinterpret_cast<const char*>(ij), 8);
+    f.write(reinterpret_cast<const char*>(&c.apc_score), 4);
+  }
+  f.write(reinterpret_cast<const char*>(&cp.cys_enrichment_ratio), 4);
+  f.write(reinterpret_cast<const char*>(cp.contact_probs.data()), static_cast<std::streamsize>(n * n * 4));
+  f.write(reinterpret_cast<const char*>(q3.data()), 28);
+  f.write(reinterpret_cast<const char*>(dq), sizeof(dq));
+}
+
 int main(int argc, char** argv) {
   if (argc < 2) return 2;
   const std::string cmd = argv[1];
@@ -311,6 +371,8 @@ int main(int argc, char** argv) {
       run_cosine(argv[2], argv[3], argv[4], argv[5]);
     } else if (cmd == "misuse" && argc == 3) {
       run_misuse(argv[2]);
+    } else if (cmd == "pipelines" && argc == 5) {
+      run_pipelines(argv[2], argv[3], argv[4]);
     } else {
       return 2;
     }

@@ -84,3 +84,68 @@ def test_quantized_cosine_similarity(esm, driver, tmp_path):
 def test_panics_and_io_errors(esm, driver, tmp_path):
     _, _, paths = _files(esm, tmp_path)
     run(driver, "misuse", paths["q4"])
+
+
+PIPE_SEQ = "MKTCAYIAKQRQCISFVKSHFSRQLEERLGCLIEVQAPILSC"
+
+
+@pytest.mark.gpu
+def test_pipelines_match_oracle(esm, orc, driver, tmp_path):
+    # load_model_weights(QuantizationMode::Q4_0) on an FP32 file, then run_pipeline_dms_with_mode
+    # in both modes and compute_pipeline_contacts_parallel (min separation 6, k = n clamped to
+    # [5, 50]); every output checked against the oracle run on the same Q4_0 blocks.
+    from test_gpu_contact_rank import reference_ranking
+    from test_gpu_dms import _oracle_scan, _oracle_wt_scan
+
+    cfg, t, paths = _files(esm, tmp_path)
+    out = tmp_path / "pipelines.bin"
+    run(driver, "pipelines", paths["fp32"], PIPE_SEQ, out)
+    raw = np.fromfile(out, np.uint8)
+    n, k = raw[:8].view(np.int32)
+    assert n == len(PIPE_SEQ)
+    off = 8
+
+    def take(count, dtype=np.float32):
+        nonlocal off
+        size = count * np.dtype(dtype).itemsize
+        a = raw[off:off + size].view(dtype)
+        off += size
+        return a
+
+    scans = []
+    for _ in range(2):
+        d = take(n * 20).reshape(n, 20)
+        e = take(n)
+        scans.append((d, e))
+    pairs = take(3 * k, np.int32).reshape(k, 3)
+    enr = take(1)[0]
+    cmap = take(n * n).reshape(n, n)
+    q3 = raw[off:off + 28]
+    off += 28
+    q3_dq = take(64)
+    assert off == raw.size
+
+    tq = esm.quantize_tensors(t, esm.DTYPE_Q4_0)
+    residues = esm.tokenize(PIPE_SEQ)[1:-1].astype(np.int32)
+    for (got_d, got_e), (window, stride, scan) in zip(
+            scans, [(0, 0, _oracle_scan), (16, 5, _oracle_wt_scan)]):
+        args = (window,) if scan is _oracle_scan else (window, stride)
+        ref_d, ref_e = scan(orc, esm, cfg, esm.DTYPE_Q4_0, tq, residues, *args)
+        assert np.abs(got_d - ref_d).max() <= 8e-2
+        assert np.abs(got_e - ref_e).max() <= 5e-2
+
+    i = np.arange(cfg.n_layers * cfg.n_heads)
+    head = np.where(i % 3 == 0, 0.0, 0.05 * np.sin(0.7 * i.astype(np.float32))).astype(np.float32)
+    ref = orc.forward(cfg, esm.DTYPE_Q4_0, tq, esm.tokenize(PIPE_SEQ), contact_w=head, contact_b=-0.5)
+    assert np.abs(cmap - ref["contacts"]).max() <= CONTACT_TOL
+    # The ranking of the map the pipeline returned is exact, ties and Cys enrichment included.
+    ri, rj, rs, renr = reference_ranking(cmap, PIPE_SEQ, 6, None, 1.0)
+    assert k == ri.size
+    np.testing.assert_array_equal(pairs[:, 0], ri)
+    np.testing.assert_array_equal(pairs[:, 1], rj)
+    np.testing.assert_array_equal(pairs[:, 2].view(np.float32), rs)
+    assert enr == renr
+
+    src = np.sin(np.float32(0.37) * np.arange(64, dtype=np.float32)).astype(np.float32)
+    np.testing.assert_array_equal(q3, esm.quantize_q3(src))
+    np.testing.assert_array_equal(q3_dq, orc.dequantize_q3(esm.quantize_q3(src)))
