@@ -16,6 +16,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 4,
   kDevBadArgs = 8,
   kDevTimeoutProbe = 16,
+  kDevBadToken = 32,  // a token id outside [0, vocab): embedded as zeros, reported as an argument error
 };
 
 // Every spin-wait on an mbarrier gives up after this many nanoseconds of %globaltimer.

@@ -599,7 +599,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   {
   ProfScope ps(c, s, ESM_PROF_NORM, 0.0, rowb * 6.0);
   ESM_CUDA(esm::launch_embed_ln(d_tokens, c->seq_of, c->escale, c->dtype == ESM_DTYPE_Q8_0 ? nullptr : c->emb_f32,
-                                c->w[0], T, d, ln1_w, ln1_b, c->x, c->xn, s));
+                                c->w[0], g.vocab_size, T, d, ln1_w, ln1_b, c->x, c->xn, c->d_err, s));
   }
   int64_t attn_pairs = 0;
   for (int b = 0; b < B; ++b) attn_pairs += static_cast<int64_t>(h_cu[b + 1] - h_cu[b]) * (h_cu[b + 1] - h_cu[b]);
@@ -786,6 +786,8 @@ int check_device_word(esm_ctx* c) {
   if (h != 0) {
     cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream);
     cudaStreamSynchronize(c->stream);
+    if (h == esm::kDevBadToken)
+      return fail(c, ESM_EINVAL, "a token id is outside [0, " + std::to_string(c->cfg.vocab_size) + ")");
     return fail(c, ESM_ETIMEOUT, "a device-side bounded wait gave up (code " + std::to_string(h) + ")");
   }
   return ESM_OK;
@@ -1145,6 +1147,7 @@ int esm_contact_top_pairs(esm_ctx* c, const float* d_map, int32_t n, const char*
     return fail(c, ESM_EINVAL, "null argument");
   // compute_pipeline_contacts_parallel asserts n >= 4 (src/pipeline.rs:421).
   if (n < 4) return fail(c, ESM_EINVAL, "Sequence too short for contact prediction");
+  if (n > 65535) return fail(c, ESM_EINVAL, "n must be at most 65535 (32-bit pair index)");
   if (min_separation < 0) return fail(c, ESM_EINVAL, "min_separation must be >= 0");
   std::lock_guard<std::mutex> lk(c->mu);
   return contact_rank_locked(c, d_map, n, seq, min_separation, max_k, top_l_factor, pos1, pos2, score, n_out,
@@ -1164,6 +1167,10 @@ int esm_contacts_pipeline(esm_ctx* c, const char* seq, int32_t min_separation, i
   int32_t L = 0;
   if (esm::tokenize(seq, toks.data(), static_cast<int32_t>(toks.size()), &L) != ESM_OK)
     return fail(c, ESM_EINVAL, "tokenizer capacity");
+  // The pipeline indexes the n x n map by byte position (src/pipeline.rs:420, 459-461), which
+  // matches the map only when every byte is one token: "<mask>" or a multi-byte character would
+  // make it read past the (L - 2)^2 entries the forward wrote.
+  if (L - 2 != n) return fail(c, ESM_EINVAL, "the contacts pipeline needs one token per byte of the sequence");
   const int32_t cu[2] = {0, L};
   int rc = validate_call(c, cu, 1, true);
   if (rc) return rc;
@@ -1355,6 +1362,8 @@ int esm_dms_wildtype_marginal(esm_ctx* c, const int32_t* residues, int32_t n, in
   if (n <= 0) return fail(c, ESM_EINVAL, "Sequence cannot be empty");
   std::lock_guard<std::mutex> lk(c->mu);
   if (!c->loaded) return fail(c, ESM_EINVAL, "no weights loaded");
+  for (int32_t i = 0; i < n; ++i)  // the wild-type ids index the logits rows
+    if (residues[i] < 0 || residues[i] >= c->cfg.vocab_size) return fail(c, ESM_EINVAL, "residue token id out of range");
   if (c->cap_tokens == 0) return fail(c, ESM_EINVAL, "call esm_reserve before the first forward");
   ESM_CUDA(cudaSetDevice(c->device));
   cudaStream_t s = c->stream;
@@ -1445,6 +1454,8 @@ int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int3
   if (n <= 0) return fail(c, ESM_EINVAL, "Sequence cannot be empty");
   std::lock_guard<std::mutex> lk(c->mu);
   if (!c->loaded) return fail(c, ESM_EINVAL, "no weights loaded");
+  for (int32_t i = 0; i < n; ++i)  // the wild-type ids index the logits rows
+    if (residues[i] < 0 || residues[i] >= c->cfg.vocab_size) return fail(c, ESM_EINVAL, "residue token id out of range");
   if (c->cap_tokens == 0) return fail(c, ESM_EINVAL, "call esm_reserve before the first forward");
   ESM_CUDA(cudaSetDevice(c->device));
   cudaStream_t s = c->stream;

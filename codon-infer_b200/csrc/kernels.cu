@@ -87,13 +87,17 @@ __global__ void seq_setup_kernel(const int32_t* __restrict__ tokens, const int32
 template <int NCH>
 __global__ void embed_ln_kernel(const int32_t* __restrict__ tokens, const int32_t* __restrict__ seq_of,
                                 const float* __restrict__ embed_scale, const float* __restrict__ emb_f32,
-                                const uint8_t* __restrict__ emb_q8, int T, int d,
+                                const uint8_t* __restrict__ emb_q8, int V, int T, int d,
                                 const float* __restrict__ ln_w, const float* __restrict__ ln_b, float* __restrict__ x,
-                                __half* __restrict__ xn) {
+                                __half* __restrict__ xn, int* err) {
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
-  const int tok = tokens[row];
+  int tok = tokens[row];
+  if (tok < 0 || tok >= V) {
+    if (lane == 0) atomicOr(err, kDevBadToken);
+    tok = 32;  // zeros, like <mask>
+  }
   const float sc = embed_scale[seq_of[row]];
   const int nchunks = (d / 4 - lane + 31) / 32;
   float4 v[NCH];
@@ -569,13 +573,13 @@ cudaError_t launch_seq_setup(const int32_t* tokens, const int32_t* cu_seqlens, i
 }
 
 cudaError_t launch_embed_ln(const int32_t* tokens, const int32_t* seq_of, const float* embed_scale,
-                            const float* emb_f32, const void* emb_q8, int T, int d, const float* ln_w,
-                            const float* ln_b, float* x, __half* xn, cudaStream_t s) {
+                            const float* emb_f32, const void* emb_q8, int V, int T, int d, const float* ln_w,
+                            const float* ln_b, float* x, __half* xn, int* err, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (d % 32 || d > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
   row_dispatch(d, [&](auto nch) {
     embed_ln_kernel<decltype(nch)::value><<<row_blocks(T), 32 * kRowWarps, 0, s>>>(
-        tokens, seq_of, embed_scale, emb_f32, static_cast<const uint8_t*>(emb_q8), T, d, ln_w, ln_b, x, xn);
+        tokens, seq_of, embed_scale, emb_f32, static_cast<const uint8_t*>(emb_q8), V, T, d, ln_w, ln_b, x, xn, err);
   });
   return cudaGetLastError();
 }

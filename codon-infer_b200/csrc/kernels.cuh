@@ -29,10 +29,11 @@ cudaError_t launch_seq_setup(const int32_t* tokens, const int32_t* cu_seqlens, i
                              float* embed_scale, cudaStream_t s);
 
 // x[t] = E[tok]*scale (0 for <mask>) in fp32, then xn = LN(x; ln_w, ln_b) in fp16.
-// E is fp32 [V, d] (emb_f32 != null) or BlockQ8_0 blocks [V, d/32] (emb_q8).
+// E is fp32 [V, d] (emb_f32 != null) or BlockQ8_0 blocks [V, d/32] (emb_q8). A token id outside
+// [0, V) is never used as an index: its row is embedded as zeros and kDevBadToken is set in *err.
 cudaError_t launch_embed_ln(const int32_t* tokens, const int32_t* seq_of, const float* embed_scale,
-                            const float* emb_f32, const void* emb_q8, int T, int d, const float* ln_w,
-                            const float* ln_b, float* x, __half* xn, cudaStream_t s);
+                            const float* emb_f32, const void* emb_q8, int V, int T, int d, const float* ln_w,
+                            const float* ln_b, float* x, __half* xn, int* err, cudaStream_t s);
 
 // out16 = LN(x) in fp16 (row stride ld16) and, when out32 != null, also in fp32 ([T, d]).
 cudaError_t launch_layernorm(const float* x, int T, int d, const float* w, const float* b, __half* out16, int ld16,

@@ -101,7 +101,7 @@ int esm_tokenize(const char* seq, int32_t* out, int32_t cap, int32_t* n_out);
  * j >= i + min_separation, in descending probability with ties in (i, j) order (the reference's
  * stable sort), the first k of them into pos1/pos2/score (host arrays of k entries; *n_out = k),
  * where k = min(max_k, #candidates) for max_k >= 0, else round(n * top_l_factor) clamped to [5, 50]
- * and to #candidates; k may not exceed 4096. seq holds the n residue letters (host memory);
+ * and to #candidates; k may not exceed 4096, n not 65535. seq holds the n residue letters (host memory);
  * *cys_enrichment = (Cys-Cys share of the k pairs) / (Cys-Cys share of all candidates), computed in
  * f32 as the reference does. The map is not copied to the host. */
 int esm_contact_top_pairs(esm_ctx* ctx, const float* d_map, int32_t n, const char* seq, int32_t min_separation,
@@ -109,7 +109,8 @@ int esm_contact_top_pairs(esm_ctx* ctx, const float* d_map, int32_t n, const cha
                           int32_t* n_out, float* cys_enrichment);
 
 /* compute_pipeline_contacts_parallel (src/pipeline.rs:410-512) for one sequence in one call: seq is
- * the residue string (n >= 4 letters, tokenized as Tokenizer::encode); the forward with contacts
+ * the residue string (n >= 4 letters, tokenized as Tokenizer::encode, one token per byte: "<mask>"
+ * or a multi-byte character is ESM_EINVAL, since the pipeline indexes the map by byte); the forward with contacts
  * (contact head set, workspace reserved for n + 2 tokens with contacts) and the ranking of
  * esm_contact_top_pairs run on the GPU, so the map crosses to the host only when contact_probs
  * ([n, n], host) is given; logits ([n + 2, vocab], host) is optional too. Outputs as in

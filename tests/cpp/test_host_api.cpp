@@ -317,6 +317,14 @@ static void run_pipelines(const std::string& f32, const std::string& seq, const 
   const ContactsPipelineResult cp = compute_pipeline_contacts_parallel(rec, 6, 1.0f, std::nullopt, cfg, w, 8);
   CHECK(cp.sequence_length == n && cp.contact_probs.size() == n * n);
   for (const ContactPair& c : cp.top_contacts) CHECK(c.pos2 >= c.pos1 + 6 && c.res1 == seq[c.pos1]);
+  // "<mask>" makes the byte count differ from the token count: refused, not misindexed.
+  bool threw = false;
+  try {
+    compute_pipeline_contacts_parallel(FastaRecord{"m", "", "MKT<mask>AYIAKQRQ"}, 6, 1.0f, std::nullopt, cfg, w, 8);
+  } catch (const std::exception&) {
+    threw = true;
+  }
+  CHECK(threw);
   // Q3_LUT blocks through the C++ types: a block decodes to the reference's LUT values.
   std::vector<float> src(64);
   for (size_t i = 0; i < src.size(); ++i) src[i] = std::sin(0.37f * static_cast<float>(i));

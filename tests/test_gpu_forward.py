@@ -216,6 +216,33 @@ def test_capacity_and_argument_errors(esm):
     m.check_device()
 
 
+def test_out_of_range_token_ids_are_rejected(esm):
+    # Tokenizer::encode only yields ids in [0, 33); an id outside is never used as an embedding
+    # index: the forward reports ESM_EINVAL and the context stays usable.
+    cfg = esm.EsmConfig(320, 1280, 1, 20, arch=0)
+    m, _, _ = build(esm, cfg, esm.DTYPE_FP32, contact=False)
+    m.reserve(200, 4, 60)
+    good = esm.random_sequences(2, 50)
+    ref = m.forward(good)["logits"]
+    for bad_id in (33, -1, 1 << 30):
+        bad = [s.copy() for s in good]
+        bad[1][7] = bad_id
+        with pytest.raises(esm.EsmError) as e:
+            m.forward(bad)
+        assert e.value.code == esm.ESM_EINVAL
+        np.testing.assert_array_equal(m.forward(good)["logits"], ref)
+    residues = good[0][1:-1].copy()
+    residues[3] = 40
+    with pytest.raises(esm.EsmError) as e:
+        m.dms_masked_marginal(residues)
+    assert e.value.code == esm.ESM_EINVAL
+    with pytest.raises(esm.EsmError) as e:
+        m.dms_wildtype_marginal(residues, 0, 0)
+    assert e.value.code == esm.ESM_EINVAL
+    m.check_device()
+    m.close()
+
+
 def test_device_wait_timeout_reports_and_recovers(esm):
     # A bounded device wait that nothing satisfies gives up after 50 ms, sets the context's error
     # word, and the host sees ESM_ETIMEOUT; the context then runs a forward normally.

@@ -2,7 +2,9 @@
 (esm_load_host_quantized, esm_load_file_quantized): the blocks must be byte-identical to the host
 quantizers (themselves pinned to the reference's BlockQ8_0/BlockQ4_0::quantize by the CPU tests),
 and a model quantized on the device must produce exactly the logits of the same model quantized
-on the host (EsmWeights::quantize_q8 / quantize_q4 then load)."""
+on the host (EsmWeights::quantize_q8 / quantize_q4 then load). For Q3_LUT (EsmWeights::quantize_q3)
+the fc1 / fc2 blocks come from the host quantizer and the attention matrices, which that model
+keeps in Q4_0, from the device one."""
 import numpy as np
 import pytest
 
@@ -69,7 +71,8 @@ def test_device_quantizer_rejects_bad_arguments(esm):
         esm.quantize_device(esm.DTYPE_Q8_0, src.data_ptr() + 4, 32, dst.data_ptr())  # src not 16-byte aligned
 
 
-@pytest.mark.parametrize("dtype_name,shape", [("DTYPE_Q8_0", "esm2_35m"), ("DTYPE_Q4_0", "esm2_650m")])
+@pytest.mark.parametrize("dtype_name,shape", [("DTYPE_Q8_0", "esm2_35m"), ("DTYPE_Q4_0", "esm2_650m"),
+                                              ("DTYPE_Q3_LUT", "esm2_150m")])
 def test_device_quantized_model_matches_host_quantized(esm, tmp_path, dtype_name, shape):
     dtype = getattr(esm, dtype_name)
     base = getattr(esm, shape)()
