@@ -130,6 +130,9 @@ struct esm_ctx {
   size_t padded_tok_cap = 0;
   float* d_padded_out = nullptr;
   size_t padded_out_cap = 0;
+  // per-layer residual states of esm_forward_ext (grows on demand)
+  float* d_layers = nullptr;
+  size_t layer_cap = 0;
   // mutational-scan staging (grows on demand): tok_row, wt_tok, deltas, entropy
   void* d_dms = nullptr;
   size_t dms_cap = 0;
@@ -828,6 +831,15 @@ int esm_config_preset(int32_t arch, esm_config* out) {
   return ESM_OK;
 }
 
+int esm_get_config(const esm_ctx* c, esm_config* out, int32_t* dtype) {
+  if (!c || !out) return ESM_EINVAL;
+  std::lock_guard<std::mutex> lk(const_cast<esm_ctx*>(c)->mu);
+  if (!c->loaded) return ESM_EINVAL;
+  *out = c->cfg;
+  if (dtype) *dtype = c->dtype;
+  return ESM_OK;
+}
+
 int esm_config_detect_file(const char* path, esm_config* out, int32_t* dtype) {
   if (!path || !out) return ESM_EINVAL;
   std::ifstream f(path, std::ios::binary | std::ios::ate);
@@ -912,6 +924,7 @@ int esm_ctx_destroy(esm_ctx* c) {
     if (c->d_rank) cudaFree(c->d_rank);
     if (c->d_padded_tokens) cudaFree(c->d_padded_tokens);
     if (c->d_padded_out) cudaFree(c->d_padded_out);
+    if (c->d_layers) cudaFree(c->d_layers);
     if (c->d_dms) cudaFree(c->d_dms);
     if (c->plan_ev) cudaEventDestroy(c->plan_ev);
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
@@ -1302,8 +1315,11 @@ int esm_forward_device(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu_
   return ESM_OK;
 }
 
-int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax, float* logits,
-                float* hidden, float* contacts) {
+namespace {
+
+// esm_forward and esm_forward_ext: padded host batch in, padded host outputs out.
+int forward_host(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax, float* logits,
+                 float* hidden, float* contacts, float* layer_hidden) {
   if (!c || !tokens || !lengths || !logits) return fail(c, ESM_EINVAL, "null argument");
   std::lock_guard<std::mutex> lk(c->mu);
   if (B <= 0 || Lmax <= 0) return fail(c, ESM_EINVAL, "empty batch");
@@ -1326,7 +1342,17 @@ int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32
     c->padded_tok_cap = ntok;
   }
   const size_t np = Lmax > 2 ? static_cast<size_t>(Lmax - 2) : 0;
-  const size_t out_need = std::max({ntok * g.vocab_size, hidden ? ntok * g.dim : 0, contacts ? B * np * np : 0});
+  const size_t out_need = std::max({ntok * g.vocab_size, (hidden || layer_hidden) ? ntok * g.dim : 0,
+                                     contacts ? B * np * np : 0});
+  // The per-layer residual states [n_layers, T, dim] (packed) are kept only while asked for.
+  const size_t layer_need = layer_hidden ? static_cast<size_t>(g.n_layers) * cu[B] * g.dim : 0;
+  if (layer_need > c->layer_cap) {
+    if (c->d_layers) cudaFree(c->d_layers);
+    c->d_layers = nullptr;
+    c->layer_cap = 0;
+    ESM_CUDA(cudaMalloc(&c->d_layers, layer_need * sizeof(float)));
+    c->layer_cap = layer_need;
+  }
   if (out_need > c->padded_out_cap) {
     if (c->d_padded_out) cudaFree(c->d_padded_out);
     c->d_padded_out = nullptr;
@@ -1340,8 +1366,15 @@ int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32
   ESM_CUDA(cudaMemcpyAsync(c->d_padded_tokens, tokens, ntok * sizeof(int32_t), cudaMemcpyHostToDevice, s));
   ESM_CUDA(esm::launch_gather_tokens(c->d_padded_tokens, c->cu, B, Lmax, c->tokens, s));
   rc = forward_impl(c, c->tokens, cu.data(), B, c->logits, hidden ? c->hidden : nullptr, contacts ? c->cmap : nullptr,
-                    nullptr, s);
+                    layer_hidden ? c->d_layers : nullptr, s);
   if (rc) return rc;
+  for (int l = 0; layer_hidden && l < g.n_layers; ++l) {
+    // Layer by layer through the padded staging buffer: [n_layers, B, Lmax, dim] on the host.
+    ESM_CUDA(esm::launch_scatter_rows(c->d_layers + static_cast<size_t>(l) * cu[B] * g.dim, c->cu, B, Lmax, g.dim,
+                                      c->d_padded_out, s));
+    ESM_CUDA(cudaMemcpyAsync(layer_hidden + static_cast<size_t>(l) * ntok * g.dim, c->d_padded_out,
+                             ntok * g.dim * sizeof(float), cudaMemcpyDeviceToHost, s));
+  }
   ESM_CUDA(esm::launch_scatter_rows(c->logits, c->cu, B, Lmax, g.vocab_size, c->d_padded_out, s));
   ESM_CUDA(cudaMemcpyAsync(logits, c->d_padded_out, ntok * g.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, s));
   if (hidden) {
@@ -1354,6 +1387,18 @@ int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32
   }
   ESM_CUDA(cudaStreamSynchronize(s));
   return check_device_word(c);
+}
+
+}  // namespace
+
+int esm_forward(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax, float* logits,
+                float* hidden, float* contacts) {
+  return forward_host(c, tokens, lengths, B, Lmax, logits, hidden, contacts, nullptr);
+}
+
+int esm_forward_ext(esm_ctx* c, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax, float* logits,
+                    float* hidden, float* contacts, float* layer_hidden) {
+  return forward_host(c, tokens, lengths, B, Lmax, logits, hidden, contacts, layer_hidden);
 }
 
 int esm_dms_wildtype_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, int32_t stride,

@@ -97,6 +97,7 @@ def lib() -> ctypes.CDLL:
         sig = {
             "esm_config_preset": [i32, vp],
             "esm_config_detect_file": [ctypes.c_char_p, vp, vp],
+            "esm_get_config": [vp, vp, vp],
             "esm_quantize_q8": [vp, i64, vp],
             "esm_quantize_q4": [vp, i64, vp],
             "esm_quantize_q3": [vp, i64, vp],
@@ -112,6 +113,7 @@ def lib() -> ctypes.CDLL:
             "esm_set_contact_head": [vp, vp, i32, f32],
             "esm_reserve": [vp, i32, i32, i32, i32],
             "esm_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
+            "esm_forward_ext": [vp, vp, vp, i32, i32, vp, vp, vp, vp],
             "esm_forward_device": [vp, vp, vp, i32, vp, vp, vp, vp, vp, i32],
             "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
             "esm_dms_masked_marginal": [vp, vp, i32, i32, vp, vp],
@@ -335,7 +337,7 @@ class Model:
         c = cfg.c_struct() if cfg else None
         self._chk(lib().esm_load_file_quantized(self._ctx, str(path).encode(), ctypes.byref(c) if c else None, dtype),
                   "esm_load_file_quantized")
-        self.cfg = cfg or detect_file(path)[0]
+        self.cfg = self.loaded_config()[0]
 
     def contact_top_pairs(self, d_map: int, n: int, seq: str, min_separation: int = 6,
                           max_k: int | None = None, top_l_factor: float = 1.0) -> dict:
@@ -357,7 +359,15 @@ class Model:
     def load_file(self, path: str, cfg: EsmConfig | None = None) -> None:
         c = cfg.c_struct() if cfg else None
         self._chk(lib().esm_load_file(self._ctx, str(path).encode(), ctypes.byref(c) if c else None), "esm_load_file")
-        self.cfg = cfg or detect_file(path)[0]
+        self.cfg = self.loaded_config()[0]
+
+    def loaded_config(self) -> tuple[EsmConfig, int]:
+        """The configuration and storage type of the loaded weights (a CODQ header's, when the
+        file has one)."""
+        c = _Config()
+        dt = ctypes.c_int32(0)
+        self._chk(lib().esm_get_config(self._ctx, ctypes.byref(c), ctypes.byref(dt)), "esm_get_config")
+        return EsmConfig(c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.vocab_size, c.max_seq_len, c.arch), dt.value
 
     def set_contact_head(self, w, b: float) -> None:
         w = np.ascontiguousarray(w, dtype=np.float32)
@@ -368,15 +378,16 @@ class Model:
 
     def forward(self, seqs, lengths=None, want_hidden: bool = False, want_contacts: bool = False,
                 logits_out: np.ndarray | None = None, hidden_out: np.ndarray | None = None,
-                contacts_out: np.ndarray | None = None) -> dict:
+                contacts_out: np.ndarray | None = None, want_layers: bool = False) -> dict:
         """Batched forward_bidirectional from host memory.
 
         `seqs` is a list of int token arrays, or a right-padded int32 [B, Lmax] array together with
         `lengths`. `logits_out`, `hidden_out` and `contacts_out` may be preallocated (e.g. pinned)
         float32 arrays of shape [B, Lmax, vocab], [B, Lmax, dim] and [B, Lmax - 2, Lmax - 2]; a
         contact map of a long batch is large (536 MB for 8 x 4096), and copying it into fresh
-        pageable memory on every call costs more than the forward. Returns padded outputs; padding
-        positions are zero."""
+        pageable memory on every call costs more than the forward. `want_layers` adds "layers", the
+        residual stream after every layer [n_layers, B, Lmax, dim] (the on_layer hook of the
+        reference's _ext forwards). Returns padded outputs; padding positions are zero."""
         if isinstance(seqs, np.ndarray) and seqs.ndim == 2:
             tokens = np.ascontiguousarray(seqs, dtype=np.int32)
             lengths = np.ascontiguousarray(lengths, dtype=np.int32)
@@ -400,9 +411,16 @@ class Model:
             np_ = max(Lmax - 2, 0)
             contacts = contacts_out if contacts_out is not None else np.empty((B, np_, np_), dtype=np.float32)
             assert contacts.shape == (B, np_, np_) and contacts.dtype == np.float32 and contacts.flags.c_contiguous
-        self._chk(lib().esm_forward(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits_out), _p(hidden),
-                                    _p(contacts)), "esm_forward")
+        if want_layers:
+            layers = np.empty((cfg.n_layers, B, Lmax, cfg.dim), dtype=np.float32)
+            self._chk(lib().esm_forward_ext(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits_out), _p(hidden),
+                                            _p(contacts), _p(layers)), "esm_forward_ext")
+        else:
+            self._chk(lib().esm_forward(self._ctx, _p(tokens), _p(lengths), B, Lmax, _p(logits_out), _p(hidden),
+                                        _p(contacts)), "esm_forward")
         res = {"logits": logits_out, "lengths": lengths}
+        if want_layers:
+            res["layers"] = layers
         if want_hidden:
             res["hidden"] = hidden
         if want_contacts:

@@ -18,6 +18,7 @@
 #include <cstdint>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <limits>
 #include <memory>
 #include <optional>
@@ -389,8 +390,14 @@ struct BidirectionalRunState {
         contact_probs(max_len_ * max_len_) {}
 };
 
+// The on_layer hook of the _ext forwards (Option<&mut dyn FnMut(usize, &[f32])>): called with the
+// layer index and the residual stream after that layer, seq_len * dim floats. An empty function is
+// None.
+using OnLayer = std::function<void(size_t, const float*, size_t)>;
+
 namespace detail {
-inline void run(const std::vector<size_t>& tokens, DeviceWeights& w, BidirectionalRunState& state) {
+inline void run(const std::vector<size_t>& tokens, DeviceWeights& w, BidirectionalRunState& state,
+                const OnLayer& on_layer = nullptr) {
   const size_t L = tokens.size();
   if (L > state.max_len)  // src/lib.rs:5106 (assert!)
     throw std::logic_error("Sequence length " + std::to_string(L) + " exceeds max_len " +
@@ -402,8 +409,20 @@ inline void run(const std::vector<size_t>& tokens, DeviceWeights& w, Bidirection
   std::vector<int32_t> toks(tokens.begin(), tokens.end());
   const int32_t len = static_cast<int32_t>(L);
   std::vector<float> cmap(contacts ? n * n : 0);
-  w.check(esm_forward(w.ctx(), toks.data(), &len, 1, len, state.logits.data(), state.x.data(),
-                      contacts ? cmap.data() : nullptr));
+  if (on_layer) {
+    // The states of all layers come back with the forward; the hook then sees them in layer
+    // order, with the same arguments as the reference's in-loop calls (src/lib.rs:5368-5370).
+    esm_config loaded{};
+    w.check(esm_get_config(w.ctx(), &loaded, nullptr));
+    const size_t nl = static_cast<size_t>(loaded.n_layers), slice = L * static_cast<size_t>(loaded.dim);
+    std::vector<float> layers(nl * slice);
+    w.check(esm_forward_ext(w.ctx(), toks.data(), &len, 1, len, state.logits.data(), state.x.data(),
+                            contacts ? cmap.data() : nullptr, layers.data()));
+    for (size_t l = 0; l < nl; ++l) on_layer(l, layers.data() + l * slice, slice);
+  } else {
+    w.check(esm_forward(w.ctx(), toks.data(), &len, 1, len, state.logits.data(), state.x.data(),
+                        contacts ? cmap.data() : nullptr));
+  }
   if (contacts) std::copy(cmap.begin(), cmap.end(), state.contact_probs.begin());
 }
 }  // namespace detail
@@ -429,6 +448,22 @@ inline void forward_bidirectional_q4(const std::vector<size_t>& tokens, const Es
 inline void forward_bidirectional_q3(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeightsQ3& w,
                                      BidirectionalRunState& state, size_t /*num_threads*/) {
   detail::run(tokens, w, state);
+}
+// The _ext forms (src/lib.rs:5097-5103, 5800-5807, 6159-6165): the same forward, plus on_layer.
+inline void forward_bidirectional_parallel_ext(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/,
+                                               EsmWeights& w, BidirectionalRunState& state, size_t /*num_threads*/,
+                                               const OnLayer& on_layer) {
+  detail::run(tokens, w, state, on_layer);
+}
+inline void forward_bidirectional_q4_ext(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeightsQ4& w,
+                                         BidirectionalRunState& state, size_t /*num_threads*/,
+                                         const OnLayer& on_layer) {
+  detail::run(tokens, w, state, on_layer);
+}
+inline void forward_bidirectional_q3_ext(const std::vector<size_t>& tokens, const EsmConfig& /*cfg*/, EsmWeightsQ3& w,
+                                         BidirectionalRunState& state, size_t /*num_threads*/,
+                                         const OnLayer& on_layer) {
+  detail::run(tokens, w, state, on_layer);
 }
 
 // ---- pipelines (src/pipeline.rs) ---------------------------------------------------------------

@@ -71,6 +71,10 @@ int esm_config_preset(int32_t arch, esm_config* out);
  * (FP32 for header-less files). */
 int esm_config_detect_file(const char* path, esm_config* out, int32_t* dtype);
 
+/* The configuration and storage type of the weights loaded into ctx (ESM_EINVAL before a load);
+ * with a CODQ header it is the header's, which may differ from the config a loader was given. */
+int esm_get_config(const esm_ctx* ctx, esm_config* out, int32_t* dtype);
+
 /* ---- quantizers (bit-exact with the reference) ---------------------------------------------- */
 
 /* quantize_slice_to_q8 / BlockQ8_0::quantize, src/lib.rs:648-673: n % 32 == 0,
@@ -167,6 +171,14 @@ int esm_reserve(esm_ctx* ctx, int32_t max_tokens, int32_t max_seqs, int32_t max_
  * Padding positions of the outputs are set to 0. */
 int esm_forward(esm_ctx* ctx, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax,
                 float* logits, float* hidden, float* contacts);
+
+/* esm_forward plus the residual stream after every layer, the values the on_layer hook of
+ * forward_bidirectional_parallel_ext / _q4_ext / _q3_ext receives (src/lib.rs:5097-5103, 5368-5370,
+ * 5800-5807, 6159-6165): layer_hidden [n_layers, B, Lmax, dim] (host, padding positions zero) or
+ * NULL, which makes the call identical to esm_forward. The states are kept on the device only
+ * while a call asks for them. */
+int esm_forward_ext(esm_ctx* ctx, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax,
+                    float* logits, float* hidden, float* contacts, float* layer_hidden);
 
 /* Same forward on DEVICE buffers of the context's GPU, packed (varlen) layout:
  *   d_tokens [T] with T = sum of lengths; h_cu_seqlens [B+1] host prefix sums of the lengths.

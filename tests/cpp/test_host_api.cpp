@@ -4,11 +4,15 @@
 //   test_host_api cpu <scratch dir>                 known-answer tests that need no GPU
 //   test_host_api forward <file> <fp32|q8|q4> <sequence> <out.bin> <contacts 0|1> <max_len>
 //                                                   one forward_bidirectional* call; writes
-//                                                   int32 L, vocab, n then logits [L, vocab] and
-//                                                   contacts [n, n] for the Python side to compare
+//                                                   int32 L, vocab, n then logits [L, vocab],
+//                                                   contacts [n, n], int32 n_layers and the _ext
+//                                                   hook's states [n_layers, L, dim] (none for Q8)
 //   test_host_api cosine <fp32 file> <q8 file> <q4 file> <sequence>
 //                                                   FP32 vs Q8_0 / Q4_0 logit cosine similarity
 //   test_host_api misuse <q4 file>                  the reference's panics and io errors
+//   test_host_api pipelines <fp32 file> <sequence> <out.bin>
+//                                                   load_model_weights(Q4_0), both DMS modes, the
+//                                                   contacts pipeline and Q3_LUT blocks
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -188,12 +192,33 @@ static void run_forward(const std::string& path, const std::string& seq, bool co
     }
     CHECK(h > 0.1f);
   }
+  // The _ext forms (FP32 and Q4_0 have one): the same outputs, and on_layer once per layer, in
+  // order, with the residual stream after that layer.
+  std::vector<float> layers;
+  int32_t nl_out = 0;
+  if constexpr (!std::is_same<W, EsmWeightsQ8>::value) {
+    BidirectionalRunState st2(cfg, max_len);
+    st2.compute_contacts = contacts;
+    size_t next = 0;
+    const OnLayer hook = [&](size_t l, const float* x, size_t count) {
+      CHECK(l == next++ && count == tokens.size() * cfg.dim);
+      layers.insert(layers.end(), x, x + count);
+    };
+    if constexpr (std::is_same<W, EsmWeights>::value) forward_bidirectional_parallel_ext(tokens, cfg, *w, st2, 8, hook);
+    else forward_bidirectional_q4_ext(tokens, cfg, *w, st2, 8, hook);
+    CHECK(next == cfg.n_layers);
+    CHECK(std::equal(st2.logits.begin(), st2.logits.begin() + L * V, state.logits.begin()));
+    CHECK(std::equal(st2.x.begin(), st2.x.begin() + static_cast<size_t>(L) * cfg.dim, state.x.begin()));
+    nl_out = static_cast<int32_t>(cfg.n_layers);
+  }
   std::ofstream f(out, std::ios::binary);
   f.write(reinterpret_cast<const char*>(&L), 4);
   f.write(reinterpret_cast<const char*>(&V), 4);
   f.write(reinterpret_cast<const char*>(&n), 4);
   f.write(reinterpret_cast<const char*>(state.logits.data()), static_cast<std::streamsize>(L) * V * 4);
   if (n > 0) f.write(reinterpret_cast<const char*>(state.contact_probs.data()), static_cast<std::streamsize>(n) * n * 4);
+  f.write(reinterpret_cast<const char*>(&nl_out), 4);
+  f.write(reinterpret_cast<const char*>(layers.data()), static_cast<std::streamsize>(layers.size() * 4));
 }
 
 static float cosine_canonical(const std::vector<float>& a, const std::vector<float>& b, size_t L, size_t V) {

@@ -195,6 +195,16 @@ def test_device_api_layer_states_and_mask_scale(esm, orc):
         for l in range(cfg.n_layers):
             scale = np.abs(states[l]).max()
             assert np.abs(ls[l, a:b] - states[l]).max() <= 1e-2 * max(scale, 1.0)
+    lc, ldt = m.loaded_config()
+    assert (lc.dim, lc.n_layers, lc.n_heads, ldt) == (cfg.dim, cfg.n_layers, cfg.n_heads, esm.DTYPE_Q4_0)
+    # The host-buffer form (esm_forward_ext): the same states, padded per sequence.
+    out = m.forward(seqs, want_layers=True)
+    assert out["layers"].shape == (cfg.n_layers, 2, 90, cfg.dim)
+    for i, s in enumerate(seqs):
+        a, b = cu[i], cu[i + 1]
+        np.testing.assert_array_equal(out["layers"][:, i, : len(s)], ls[:, a:b])
+        assert not out["layers"][:, i, len(s):].any()
+        np.testing.assert_array_equal(out["logits"][i, : len(s)], lg[a:b])
 
 
 def test_capacity_and_argument_errors(esm):

@@ -64,14 +64,21 @@ def test_forward_matches_oracle(esm, orc, driver, tmp_path, kind):
     L, V, n = raw[:3]
     vals = raw[3:].view(np.float32)
     logits = vals[: L * V].reshape(L, V)
-    contacts = vals[L * V:].reshape(n, n)
+    contacts = vals[L * V: L * V + n * n].reshape(n, n)
+    nl = raw[3 + L * V + n * n]
+    layers = raw[4 + L * V + n * n:].view(np.float32).reshape(nl, L, cfg.dim)
+    assert nl == (0 if kind == "q8" else cfg.n_layers)  # the reference has no _q8_ext
     i = np.arange(cfg.n_layers * cfg.n_heads)
     head = np.where(i % 3 == 0, 0.0, 0.05 * np.sin(0.7 * i.astype(np.float32))).astype(np.float32)
     toks = esm.tokenize(SEQ)
-    ref = orc.forward(cfg, dtype, esm.quantize_tensors(t, dtype), toks, contact_w=head, contact_b=-0.5)
+    states = []
+    ref = orc.forward(cfg, dtype, esm.quantize_tensors(t, dtype), toks, contact_w=head, contact_b=-0.5,
+                      on_layer=lambda l, x: states.append(x))
     assert np.abs(logits - ref["logits"]).max() <= LOGIT_TOL
     assert (logits.argmax(1) == ref["logits"].argmax(1)).mean() >= 0.99
     assert np.abs(contacts - ref["contacts"]).max() <= CONTACT_TOL
+    for l in range(nl):  # on_layer of the _ext forwards
+        assert np.abs(layers[l] - states[l]).max() <= 1e-2 * max(np.abs(states[l]).max(), 1.0)
 
 
 @pytest.mark.gpu
