@@ -12,6 +12,8 @@
 //               the 128-byte-swizzled K-major layout the MMA reads. O accumulates across tiles in
 //               tensor memory; it is rescaled there only when a row max grows past the threshold.
 // Tensor memory: S in columns [0, 64), O in [64, 128). All waits are bounded.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -297,13 +299,13 @@ cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_k
                                 cudaStream_t s) {
   if (p.n_work <= 0) return cudaSuccess;
   if (p.dh != kD) return cudaErrorInvalidValue;
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(configured & (1ull << dev))) {
+  if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAt);
     if (e != cudaSuccess) return e;
-    if (dev < 64) configured |= (1ull << dev);
+    if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   dim3 grid(p.n_work, p.H);
   attention_tc_kernel<<<grid, kThreadsAt, kSmemAt, s>>>(tm_q, tm_kv, p);

@@ -16,6 +16,8 @@
 // so the next S of a tile starts as soon as its P has been written, while the other tile's
 // softmax runs. O is rescaled in tensor memory only when a row max grows past the threshold.
 // All waits are bounded.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -320,14 +322,14 @@ __global__ void __launch_bounds__(kThreads2, 2)
 
 template <int DH, int POLY>
 cudaError_t launch_poly(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p, cudaStream_t s) {
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(configured & (1ull << dev))) {
+  if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(attention_tc2_kernel<DH, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Tc2<DH>::kSmem);
     if (e != cudaSuccess) return e;
-    if (dev < 64) configured |= (1ull << dev);
+    if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   dim3 grid(p.n_work, p.H);
   attention_tc2_kernel<DH, POLY><<<grid, kThreads2, Tc2<DH>::kSmem, s>>>(tm_q, tm_kv, p);

@@ -24,6 +24,8 @@
 // outstanding, and a parity wait for PV(n - 1) would match the completed phase of PV(n - 3).)
 // O is rescaled in tensor memory only when a row max grows past the threshold, after PV(j - 1) has
 // completed. All waits are bounded.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -377,14 +379,14 @@ __global__ void __launch_bounds__(kThreads3, 2)
 
 template <int DH, int POLY, int EXP>
 cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p, cudaStream_t s) {
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(configured & (1ull << dev))) {
+  if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(attention_tc3_kernel<DH, POLY, EXP>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Tc3<DH>::kSmem);
     if (e != cudaSuccess) return e;
-    if (dev < 64) configured |= (1ull << dev);
+    if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   dim3 grid(p.n_work, p.H);
   attention_tc3_kernel<DH, POLY, EXP><<<grid, kThreads3, Tc3<DH>::kSmem, s>>>(tm_q, tm_kv32, p);

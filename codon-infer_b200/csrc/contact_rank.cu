@@ -13,6 +13,7 @@
 // Selection. Rounds of one kernel: every CTA sorts a tile of kTile keys in shared memory (bitonic
 // network, 1024 threads) and writes its first K (a power of two >= k), until one tile holds all
 // survivors; its first k keys are the answer. n^2 = 16.8 M candidates take three rounds at K = 64.
+#include <atomic>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -95,15 +96,15 @@ cudaError_t launch_contact_rank(const float* map, int n, int min_sep, int k, uin
   if (n <= 0 || k <= 0 || k > kTile / 2) return cudaErrorInvalidValue;
   int keep = 1;
   while (keep < k) keep <<= 1;
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   const int smem = kTile * static_cast<int>(sizeof(uint64_t));
-  if (dev >= 64 || !(configured & (1ull << dev))) {
+  if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(rank_map_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(rank_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    if (dev < 64) configured |= (1ull << dev);
+    if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   const int64_t tiles0 = (static_cast<int64_t>(n) * n + kTile - 1) / kTile;
   uint64_t* buf[2] = {scratch, scratch + tiles0 * keep};

@@ -27,6 +27,8 @@
 // Four S^T buffers let the MMAs run up to three heads ahead of the exponentials: with two, the
 // round trip MMA -> softmax read -> buffer release -> next MMA set the pace, not the math.
 // All waits are bounded; on a timeout the error word is set and M is left untouched.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -340,15 +342,15 @@ cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_
   if (p.n_tiles <= 0) return cudaSuccess;
   if (p.dh != kD || p.H > kMaxHeads) return cudaErrorInvalidValue;
   const int smem = contact_tc_smem_bytes(p.H);
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(configured & (1ull << dev))) {
+  if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
     // The largest head count (64) fixes the attribute once per device.
     cudaError_t e = cudaFuncSetAttribute(contact_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          contact_tc_smem_bytes(kMaxHeads));
     if (e != cudaSuccess) return e;
-    if (dev < 64) configured |= (1ull << dev);
+    if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   contact_tc_kernel<<<p.n_tiles, kThreadsCt, smem, s>>>(tm_k128, tm_q64, p);
   return cudaGetLastError();

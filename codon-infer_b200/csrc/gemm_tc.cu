@@ -20,6 +20,7 @@
 // Two accumulator buffers in tensor memory let the epilogue of tile i overlap the mainloop of
 // tile i+1. Every wait is bounded (globaltimer), so a broken pipeline reports an error instead of
 // hanging the GPU. No load is multicast.
+#include <atomic>
 #include <cstdio>
 
 #include "common.cuh"
@@ -646,13 +647,13 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
                        int num_sms, cudaStream_t stream) {
   using S = GemmShape<BN, CG, TS>;
   auto kern = gemm_tc_kernel<BN, EPI, DH, CG, TS>;
-  static unsigned long long configured = 0;  // one bit per device ordinal
+  static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(configured & (1ull << dev))) {
+  if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
     if (e != cudaSuccess) return e;
-    if (dev < 64) configured |= (1ull << dev);
+    if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -668,16 +669,16 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   // Tiles are split statically over the persistent CTAs, so every cluster must be resident at
   // once: a cluster of two needs two free SMs in one GPC, and the count of clusters that fit at the
   // same time can be below num_sms / 2.
-  static int resident[64] = {0};
+  static std::atomic<int> resident[64] = {};
   int max_clusters = num_sms / CG;
   if (CG > 1 && dev < 64) {
-    if (resident[dev] == 0) {
+    int n = resident[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
       cfg.gridDim = dim3(max_clusters * CG, 1, 1);
-      int n = 0;
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = max_clusters;
-      resident[dev] = n;
+      resident[dev].store(n, std::memory_order_relaxed);
     }
-    max_clusters = resident[dev] < max_clusters ? resident[dev] : max_clusters;
+    max_clusters = n < max_clusters ? n : max_clusters;
   }
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int clusters = tiles < max_clusters ? tiles : max_clusters;

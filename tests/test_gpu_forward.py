@@ -253,6 +253,42 @@ def test_out_of_range_token_ids_are_rejected(esm):
     m.close()
 
 
+def test_concurrent_calls_from_host_threads(esm):
+    # The threading contract: calls on one context are serialised by its lock, and contexts run
+    # independently (each on its own stream). Two contexts, two host threads each (ctypes drops
+    # the GIL during the calls): every result equals the same call made alone.
+    import threading
+
+    cfg = esm.EsmConfig(320, 1280, 2, 20, arch=0)
+    models = [build(esm, cfg, esm.DTYPE_Q4_0, seed=1, contact=False)[0],
+              build(esm, cfg, esm.DTYPE_Q8_0, seed=2, contact=False)[0]]
+    for m in models:
+        m.reserve(3 * 200, 3, 200)
+    batches = [esm.random_sequences(3, [50, 120, 200], seed=40 + j) for j in range(4)]
+    ref = {(i, j): m.forward(batches[j])["logits"] for i, m in enumerate(models) for j in range(4)}
+    errors = []
+
+    def worker(i, js):
+        try:
+            for _ in range(3):
+                for j in js:
+                    if not np.array_equal(models[i].forward(batches[j])["logits"], ref[(i, j)]):
+                        errors.append(f"context {i} batch {j} differs")
+        except Exception as e:  # noqa: BLE001 -- reported below
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=worker, args=(i, js)) for i in range(2) for js in ([0, 1], [2, 3])]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not any(t.is_alive() for t in threads)
+    assert not errors, errors[:4]
+    for m in models:
+        m.check_device()
+        m.close()
+
+
 def test_device_wait_timeout_reports_and_recovers(esm):
     # A bounded device wait that nothing satisfies gives up after 50 ms, sets the context's error
     # word, and the host sees ESM_ETIMEOUT; the context then runs a forward normally.
