@@ -10,9 +10,9 @@
 // keys are unique. (NaN probabilities compare Equal to everything in the reference, which has no
 // consistent order; sigmoid outputs are never NaN.)
 //
-// Selection. Rounds of one kernel: every CTA sorts a tile of kTile keys in shared memory (bitonic
+// Selection. Passes of one kernel: every CTA sorts a tile of kTile keys in shared memory (bitonic
 // network, 1024 threads) and writes its first K (a power of two >= k), until one tile holds all
-// survivors; its first k keys are the answer. n^2 = 16.8 M candidates take three rounds at K = 64.
+// survivors; its first k keys are the answer. n^2 = 16.8 M candidates take three passes at K = 64.
 #include <atomic>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -53,7 +53,7 @@ __device__ void bitonic_sort(uint64_t* s) {
   __syncthreads();
 }
 
-// Round 0: keys straight from the map (candidates only), tile = kTile consecutive flat indices.
+// Pass 0: keys straight from the map (candidates only), tile = kTile consecutive flat indices.
 __global__ void __launch_bounds__(kRankThreads)
     rank_map_kernel(const float* __restrict__ map, int n, int min_sep, int keep, uint64_t* __restrict__ out) {
   extern __shared__ uint64_t s[];
@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kRankThreads)
   for (int t = threadIdx.x; t < keep; t += kRankThreads) out[static_cast<int64_t>(blockIdx.x) * keep + t] = s[t];
 }
 
-// Later rounds: tiles of kTile keys from the previous round's survivors.
+// Later passes: tiles of kTile keys from the previous pass's survivors.
 __global__ void __launch_bounds__(kRankThreads)
     rank_keys_kernel(const uint64_t* __restrict__ in, int64_t count, int keep, uint64_t* __restrict__ out) {
   extern __shared__ uint64_t s[];
@@ -88,7 +88,7 @@ int64_t contact_rank_scratch_keys(int n, int k) {
   int keep = 1;
   while (keep < k) keep <<= 1;
   const int64_t tiles = (static_cast<int64_t>(n) * n + kTile - 1) / kTile;
-  return 2 * tiles * keep;  // two ping-pong buffers of round-0 output size
+  return 2 * tiles * keep;  // two ping-pong buffers of pass-0 output size
 }
 
 cudaError_t launch_contact_rank(const float* map, int n, int min_sep, int k, uint64_t* scratch, uint64_t* out_keys,
