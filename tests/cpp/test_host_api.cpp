@@ -12,7 +12,7 @@
 //   test_host_api misuse <q4 file>                  the reference's panics and io errors
 //   test_host_api pipelines <fp32 file> <sequence> <out.bin>
 //                                                   load_model_weights(Q4_0), both DMS modes, the
-//                                                   contacts pipeline and Q3_LUT blocks
+//                                                   contacts and inpaint pipelines, Q3_LUT blocks
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -376,6 +376,30 @@ static void run_pipelines(const std::string& f32, const std::string& seq, const 
   f.write(reinterpret_cast<const char*>(cp.contact_probs.data()), static_cast<std::streamsize>(n * n * 4));
   f.write(reinterpret_cast<const char*>(q3.data()), 28);
   f.write(reinterpret_cast<const char*>(dq), sizeof(dq));
+
+  // compute_pipeline_inpaint_parallel on a sequence with three masks ('*' and "<mask>").
+  const std::string masked = "MKT*AYIAK*RQ<mask>ISFVKSHFSRQLEERLG";
+  const InpaintPipelineResult ip = compute_pipeline_inpaint_parallel(FastaRecord{"m", "", masked}, cfg, w, 8);
+  const std::vector<size_t> mt = Tokenizer::encode(masked);
+  CHECK(ip.sites.size() == 3 && ip.reconstructed_sequence.size() == mt.size() - 2);
+  const int32_t nsites = static_cast<int32_t>(ip.sites.size());
+  f.write(reinterpret_cast<const char*>(&nsites), 4);
+  for (const InpaintSite& site : ip.sites) {
+    CHECK(mt[site.position] == 32 && site.candidates.size() == 5);
+    CHECK(site.predicted_char == site.candidates[0].amino_acid);
+    CHECK(ip.reconstructed_sequence[site.position - 1] == site.predicted_char);
+    for (size_t k = 0; k < 5; ++k) {
+      CHECK(std::string(site.candidates[k].category) == aa_category(site.candidates[k].amino_acid));
+      if (k) CHECK(site.candidates[k].probability_pct <= site.candidates[k - 1].probability_pct);
+    }
+    const int32_t pos = static_cast<int32_t>(site.position);
+    f.write(reinterpret_cast<const char*>(&pos), 4);
+    for (const InpaintCandidate& c : site.candidates) {
+      const int32_t ch = c.amino_acid;
+      f.write(reinterpret_cast<const char*>(&ch), 4);
+    }
+    for (const InpaintCandidate& c : site.candidates) f.write(reinterpret_cast<const char*>(&c.probability_pct), 4);
+  }
 }
 
 int main(int argc, char** argv) {
