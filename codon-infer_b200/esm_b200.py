@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
             "esm_load_file_quantized": [vp, ctypes.c_char_p, vp, i32],
             "esm_quantize_device": [i32, vp, i64, vp, vp],
             "esm_contact_top_pairs": [vp, vp, i32, ctypes.c_char_p, i32, i32, f32, vp, vp, vp, vp, vp],
+            "esm_contacts_pipeline": [vp, ctypes.c_char_p, i32, i32, f32, vp, vp, vp, vp, vp, vp, vp],
             "esm_set_contact_head": [vp, vp, i32, f32],
             "esm_reserve": [vp, i32, i32, i32, i32],
             "esm_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
@@ -355,6 +356,31 @@ class Model:
                   "esm_contact_top_pairs")
         k = n_out.value
         return {"pos1": pos1[:k], "pos2": pos2[:k], "score": score[:k], "cys_enrichment": enr.value}
+
+    def contacts_pipeline(self, seq: str, min_separation: int = 6, max_k: int | None = None,
+                          top_l_factor: float = 1.0, want_map: bool = False, want_logits: bool = False) -> dict:
+        """compute_pipeline_contacts_parallel for one residue string in one call (esm_contacts_pipeline):
+        the forward with contacts and the pair ranking run on the GPU; the n x n map and the logits
+        come back only when asked for."""
+        n = len(seq.encode())
+        cap = 4096
+        pos1 = np.zeros(cap, dtype=np.int32)
+        pos2 = np.zeros(cap, dtype=np.int32)
+        score = np.zeros(cap, dtype=np.float32)
+        cmap = np.empty((n, n), dtype=np.float32) if want_map else None
+        logits = np.empty((n + 2, self.cfg.vocab_size), dtype=np.float32) if want_logits else None
+        n_out = ctypes.c_int32(0)
+        enr = ctypes.c_float(0.0)
+        self._chk(lib().esm_contacts_pipeline(self._ctx, seq.encode(), min_separation, -1 if max_k is None else max_k,
+                                              top_l_factor, _p(logits), _p(cmap), _p(pos1), _p(pos2), _p(score),
+                                              ctypes.byref(n_out), ctypes.byref(enr)), "esm_contacts_pipeline")
+        k = n_out.value
+        res = {"pos1": pos1[:k], "pos2": pos2[:k], "score": score[:k], "cys_enrichment": enr.value}
+        if want_map:
+            res["contact_probs"] = cmap
+        if want_logits:
+            res["logits"] = logits
+        return res
 
     def load_file(self, path: str, cfg: EsmConfig | None = None) -> None:
         c = cfg.c_struct() if cfg else None

@@ -86,3 +86,31 @@ def test_ranking_of_a_forward_contact_map(esm):
     np.testing.assert_array_equal(got["pos2"], p2)
     np.testing.assert_array_equal(got["score"], sc)
     assert np.float32(got["cys_enrichment"]) == enr
+
+
+def test_contacts_pipeline_one_call(esm):
+    # esm_contacts_pipeline (tokenize, forward with contacts, ranking) gives what the separate calls
+    # give on the same map, and refuses a sequence whose bytes are not one token each.
+    cfg = esm.esm2_8m()
+    m = esm.Model(0)
+    m.load_tensors(cfg, esm.DTYPE_FP32, esm.synth_fp32_tensors(cfg, seed=5))
+    rng = np.random.default_rng(6)
+    m.set_contact_head((rng.standard_normal(cfg.n_layers * cfg.n_heads) * 0.1).astype(np.float32), -0.5)
+    seq = "".join(rng.choice(list(AAS + "CC"), 150))
+    n = len(seq)
+    m.reserve(n + 2, 1, n + 2, contacts=True)
+    one = m.contacts_pipeline(seq, 6, None, 1.0, want_map=True, want_logits=True)
+    fwd = m.forward([esm.tokenize(seq)], want_contacts=True)
+    # Logits are bitwise reproducible; contact maps to float rounding (the APC row sums are
+    # accumulated across tiles with float atomics, in an order that varies between runs).
+    np.testing.assert_array_equal(one["logits"], fwd["logits"][0])
+    assert np.abs(one["contact_probs"] - fwd["contacts"][0]).max() <= 1e-6
+    p1, p2, sc, enr = reference_ranking(one["contact_probs"], seq, 6, None, 1.0)
+    np.testing.assert_array_equal(one["pos1"], p1)
+    np.testing.assert_array_equal(one["pos2"], p2)
+    np.testing.assert_array_equal(one["score"], sc)
+    assert np.float32(one["cys_enrichment"]) == enr
+    with pytest.raises(esm.EsmError) as e:
+        m.contacts_pipeline("MKT<mask>AYIAKQRQISFVK")
+    assert e.value.code == esm.ESM_EINVAL
+    m.close()
