@@ -616,6 +616,19 @@ inline InpaintPipelineResult compute_pipeline_inpaint_parallel(const FastaRecord
   return r;
 }
 
+// The convenience forms (src/pipeline.rs:33-74, 389-407, 610-617), without the terminal theme.
+inline DmsPipelineResult run_pipeline_dms_parallel(const FastaRecord& record, size_t window_size, size_t stride,
+                                                   const EsmConfig& cfg, DeviceWeights& w, size_t num_threads) {
+  return run_pipeline_dms_with_mode(record, window_size, stride, cfg, w, num_threads, DmsScoringMode::MaskedMarginal);
+}
+inline DmsPipelineResult run_pipeline_dms(const FastaRecord& record, size_t window_size, size_t stride,
+                                          const EsmConfig& cfg, EsmWeights& w) {
+  return run_pipeline_dms_parallel(record, window_size, stride, cfg, w, 1);
+}
+inline InpaintPipelineResult compute_pipeline_inpaint(const FastaRecord& record, const EsmConfig& cfg, EsmWeights& w) {
+  return compute_pipeline_inpaint_parallel(record, cfg, w, 1);
+}
+
 struct ContactPair {  // src/benchmark.rs:107-115
   size_t pos1 = 0;
   char res1 = 0;
@@ -670,6 +683,12 @@ inline ContactsPipelineResult compute_pipeline_contacts_parallel(const FastaReco
     r.top_contacts.push_back(c);
   }
   return r;
+}
+
+inline ContactsPipelineResult compute_pipeline_contacts(const FastaRecord& record, size_t min_separation,
+                                                        float top_l_factor, std::optional<size_t> max_k,
+                                                        const EsmConfig& cfg, EsmWeights& w) {
+  return compute_pipeline_contacts_parallel(record, min_separation, top_l_factor, max_k, cfg, w, 1);
 }
 
 }  // namespace codon_infer

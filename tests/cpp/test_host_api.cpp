@@ -324,6 +324,12 @@ static void run_pipelines(const std::string& f32, const std::string& seq, const 
   const FastaRecord rec{"test", "test protein", seq};
   const DmsPipelineResult mm = run_pipeline_dms_with_mode(rec, 0, 0, cfg, w, 8, DmsScoringMode::MaskedMarginal);
   const DmsPipelineResult wt = run_pipeline_dms_with_mode(rec, 16, 5, cfg, w, 8, DmsScoringMode::WildtypeMarginal);
+  {
+    // The convenience form is the masked-marginal mode.
+    const DmsPipelineResult again = run_pipeline_dms_parallel(rec, 0, 0, cfg, w, 8);
+    CHECK(again.rows.size() == mm.rows.size() && again.scoring_mode == DmsScoringMode::MaskedMarginal);
+    for (size_t p = 0; p < again.rows.size() && p < mm.rows.size(); ++p) CHECK(again.rows[p].deltas == mm.rows[p].deltas);
+  }
   const size_t n = seq.size();
   for (const DmsPipelineResult* r : {&mm, &wt}) {
     CHECK(r->rows.size() == n);
