@@ -130,6 +130,37 @@ static void test_quantize_slice_rejects_ragged_length() {
   CHECK(quantize_slice_to_q8(std::vector<float>(64, 1.0f)).size() == 2);
 }
 
+static void test_dms_row() {  // test_dms_row_and_csv_generation (src/export.rs:2603-2608), DmsPositionRow::new
+  const float zeros[20] = {0};
+  const DmsPositionRow row = DmsPositionRow::make(1, 'M', zeros, 2.5f);
+  CHECK(row.pos == 1 && row.wt == 'M' && row.mean_delta_logp == 0.0f && row.entropy == 2.5f);
+  CHECK(std::string(row.category) == "Tolerated Variable");
+  // The mean is over the 19 non-zero deltas; the thresholds are -3.8 and -2.2 (src/export.rs:16-38).
+  const std::pair<float, const char*> cases[] = {{-4.0f, "Catalytic / Strictly Intolerant"},
+                                                 {-3.0f, "Conserved Structural Core"},
+                                                 {-2.0f, "Tolerated Variable"}};
+  for (const auto& [v, want] : cases) {
+    float d[20];
+    for (float& x : d) x = v;
+    d[7] = 0.0f;  // the wild type
+    const DmsPositionRow r = DmsPositionRow::make(2, 'A', d, 1.0f);
+    CHECK(std::fabs(r.mean_delta_logp - v) < 1e-5f);
+    CHECK(std::string(r.category) == want);
+  }
+}
+
+static void test_aa_category() {  // aa_category, src/ui.rs:77-89
+  CHECK(std::string(aa_category('L')) == "Hydrophobic Aliphatic");
+  CHECK(std::string(aa_category('W')) == "Hydrophobic Aromatic");
+  CHECK(std::string(aa_category('H')) == "Basic Positively Charged");
+  CHECK(std::string(aa_category('E')) == "Acidic Negatively Charged");
+  CHECK(std::string(aa_category('Q')) == "Polar Uncharged");
+  CHECK(std::string(aa_category('C')) == "Cysteine (Disulfide / Redox)");
+  CHECK(std::string(aa_category('P')) == "Special Conformation (Loop/Kink)");
+  CHECK(std::string(aa_category('*')) == "Masked Token (<mask_1>)");
+  CHECK(std::string(aa_category('X')) == "Non-standard Residue");
+}
+
 static void test_config_presets() {  // src/lib.rs:87-150
   const EsmConfig c8 = EsmConfig::esm2_8m();
   CHECK(c8.dim == 320 && c8.hidden_dim == 1280 && c8.n_layers == 6 && c8.n_heads == 20 && c8.head_dim() == 16);
@@ -422,6 +453,8 @@ int main(int argc, char** argv) {
       test_q4_0_zero_block();
       test_quantize_slice_rejects_ragged_length();
       test_config_presets();
+      test_dms_row();
+      test_aa_category();
       test_detect_from_file_errors(argv[2]);
     } else if (cmd == "forward" && argc == 8) {
       const std::string kind = argv[3];
