@@ -350,9 +350,11 @@ def run_ours(args):
             "metric": metric_name(args.config, c, batch), "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 operands / f32 accumulate (" + ["FP32", "Q8_0", "Q4_0"][dtype] + " weights)",
+            "dtype": "f16",
             "data": "synthetic (seeded uniform residues, random-init N(0,0.02) weights)",
             "config": {"workload": c["desc"], "batch_per_gpu": batch, "seq_len": Lmax, "tokens_per_gpu": T,
+                       "arithmetic": "f16 tensor-core operands, f32 accumulate; "
+                                     + ["FP32", "Q8_0", "Q4_0"][dtype] + " weights dequantised per layer",
                        "parallelism": f"sequence-sharded x{world}, logits all-gather",
                        "l2": "no flush: the per-step working set (activations, weights) exceeds the 126 MB L2"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(host_tokens.nbytes + 4 * batch),
