@@ -1,18 +1,25 @@
 """Throughput benchmark of the B200 ESM-2 encoder forward (codon-infer's hot path).
 
-Workload (default): ESM-2 650M with Q4_0 weights (random-init N(0, 0.02), quantized by the
+Workload (default, c4): ESM-2 650M with Q4_0 weights (random-init N(0, 0.02), quantized by the
 bit-exact BlockQ4_0 quantizer), 64 sequences x L = 1024 tokens of uniform-random residues per GPU,
 logits [64, 1024, 33] out. Metric: residues/s over the whole job (tokens incl. <cls>/<eos>).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1..c5]
   torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
 
-Scaling is weak: every rank runs its own 64-sequence batch (sequences are independent), and the
-only collective is the gather of the logits to all ranks after each forward. `value` times
-device-resident inputs with CUDA events; `e2e` times the host API (esm_forward: pinned host
-tokens in, host logits out) with the copies inside the timed region. --impl reference times the
-CPU restatement of the reference forward (the reference crate is Rust and cannot be built in this
-image) on the host cores, one 1024-token sequence per step.
+Scaling. Forward configurations (c1, c2, c4, c5) are weak-scaled in `value`: every rank runs its
+own batch (sequences are independent) and the only collective is the gather of the logits after
+each forward. With N > 1 the line also carries `strong_scaling`: the one 64 x 1024 batch of c4 (the
+configuration's own "sequences are sharded across 1/2/4/8 GPUs") split into N cost-balanced
+contiguous blocks (esm_partition), each rank running its block, then the logits gathered. The
+mutational scan (c3) is strong-scaled: the 300 masked variants of the one wild type are split
+into N contiguous blocks and only the per-variant rows cross between GPUs.
+
+`value` times device-resident inputs with CUDA events; `e2e` times the host API (esm_forward, or
+esm_dms_masked_marginal_range for the scan: host buffers in and out) with the copies inside the
+timed region. --impl reference times the CPU restatement of the reference forward (the reference
+crate is Rust and cannot be built in this image) on the host cores, one sequence per step; that
+arm loads only the oracle library.
 """
 from __future__ import annotations
 
@@ -31,43 +38,16 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "codon-infer_b200"))
 
+import synth  # noqa: E402  (numpy only: no native library is loaded by this import)
+
 UNIT = "residues/s"
-# The benchmark configurations (tokens include <cls>/<eos>). c4 is the headline and the default.
-CONFIGS = {
-    "c1": dict(arch=0, dtype=0, batch=1, lengths="fixed", seq_len=128, contacts=True, dms=False,
-               desc="ESM-2 8M FP32 forward, 1 x L=128, contact head on"),
-    "c2": dict(arch=1, dtype=1, batch=32, lengths="uniform", seq_len=512, min_len=64, contacts=False, dms=False,
-               desc="ESM-2 35M Q8_0 forward, 32 sequences with L in U[64, 512], right-padded"),
-    "c3": dict(arch=2, dtype=0, batch=300, lengths="fixed", seq_len=302, contacts=False, dms=True,
-               desc="ESM-2 150M FP32 masked-marginal scan: 300 single-<mask> variants of a 300-residue wild type"),
-    "c4": dict(arch=3, dtype=2, batch=64, lengths="fixed", seq_len=1024, contacts=False, dms=False,
-               desc="ESM-2 650M Q4_0 forward, 64 x L=1024 per GPU, logits out"),
-    "c5": dict(arch=4, dtype=1, batch=8, lengths="fixed", seq_len=4096, contacts=True, dms=False,
-               desc="ESM-2 3B Q8_0 forward, 8 x L=4096 per GPU, contact maps on"),
-}
+CONFIGS = synth.CONFIGS
 
 
-def metric_name(cfg_name, c, batch):
+def metric_name(cfg_name, c):
     return {
         "c4": "residues/sec, ESM-2 650M Q4_0 forward (64 x L=1024 per GPU)",
     }.get(cfg_name, f"residues/sec, {c['desc']}")
-
-
-def workload_sequences(esm, c, batch, rank):
-    """Token sequences of one rank's batch (seeded per rank)."""
-    if c["dms"]:
-        wt = esm.random_sequences(1, c["seq_len"], seed=2000)[0]
-        out = []
-        for p in range(batch):
-            v = wt.copy()
-            v[1 + (p % (c["seq_len"] - 2))] = esm.MASK_ID
-            out.append(v)
-        return out
-    if c["lengths"] == "uniform":
-        rng = np.random.default_rng(3000 + rank)
-        lens = rng.integers(c["min_len"], c["seq_len"] + 1, size=batch)
-        return esm.random_sequences(batch, lens, seed=1000 + rank)
-    return esm.random_sequences(batch, c["seq_len"], seed=1000 + rank)
 
 
 def measured_peaks():
@@ -145,47 +125,125 @@ def physical_gpu(local_rank):
     return None
 
 
-def cpu_forward_rate(cfg, dtype, tensors, seq_len, seed, threads):
-    """Oracle forward of one sequence: residues/s on `threads` host threads."""
+def oracle_module():
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
-    import esm_b200 as esm
-    s = esm.random_sequences(1, seq_len, seed=seed)[0]
+    return oracle
+
+
+def cpu_sample(c, k):
+    """The k-th CPU sample sequence of a workload: a masked variant of the scan (c3), a sequence of
+    the ragged batch (c2), else one full-length sequence, capped at 1024 tokens (c5's 4096-token
+    sequences would take minutes each on the host)."""
+    if c["dms"]:
+        return synth.workload_sequences(c, 1, first=37 * k)[0]
+    if c["lengths"] == "uniform":
+        seqs = synth.workload_sequences(c, c["batch"])
+        return seqs[k % len(seqs)]
+    return synth.random_sequences(1, min(c["seq_len"], 1024), seed=5000 + k)[0]
+
+
+def cpu_rate(oracle, cfg, c, tensors, k0, n, threads):
+    """Oracle forwards of n sample sequences: (residues/s, residues)."""
+    res = 0
     t0 = time.perf_counter()
-    oracle.forward(cfg, dtype, tensors, s, n_threads=threads)
-    return seq_len / (time.perf_counter() - t0)
+    for k in range(k0, k0 + n):
+        s = cpu_sample(c, k)
+        cw = synth.contact_head(cfg) if c["contacts"] else None
+        oracle.forward(cfg, c["dtype"], tensors, s, n_threads=threads, contact_w=cw, contact_b=0.0)
+        res += len(s)
+    return res / (time.perf_counter() - t0), res
+
+
+def cpu_weights(oracle, c):
+    cfg = synth.preset(c["arch"])
+    t = oracle.quantize_tensors(synth.synth_fp32_tensors(cfg, seed=synth.WEIGHT_SEED), c["dtype"])
+    return cfg, t
+
+
+def cpu_sample_desc(c, cfg):
+    L = min(c["seq_len"], 1024)
+    what = {True: f"one masked variant of the {c['seq_len']}-token scan",
+            False: f"one {L}-token sequence" if c["lengths"] == "fixed" else "one sequence of the ragged batch"}[c["dms"]]
+    heads = ", contact head on" if c["contacts"] else ""
+    return f"{what} per step, full {cfg.n_layers}-layer forward{heads} (CPU restatement of the reference)"
 
 
 def run_reference(args):
-    """CPU arm: the restated reference forward on the host cores, one sequence per step."""
-    import esm_b200 as esm
+    """CPU arm: the restated reference forward on the host cores, one sequence per step. Loads the
+    oracle library only (weights quantized by the oracle's own quantizers)."""
     rank = int(os.environ.get("RANK", "0"))
     c = CONFIGS[args.config]
-    batch = args.batch or c["batch"]
     if rank != 0:
         return
-    cfg = esm.EsmConfig.preset(c["arch"])
-    t = esm.quantize_tensors(esm.synth_fp32_tensors(cfg, seed=0), c["dtype"])
+    oracle = oracle_module()
+    cfg, t = cpu_weights(oracle, c)
     threads = os.cpu_count() or 1
-    seq_len = c["seq_len"]
-    for w in range(args.warmup):
-        cpu_forward_rate(cfg, c["dtype"], t, seq_len, 1000 + w, threads)
+    cpu_rate(oracle, cfg, c, t, 0, args.warmup, threads)
     t0 = time.perf_counter()
-    for k in range(args.steps):
-        cpu_forward_rate(cfg, c["dtype"], t, seq_len, 2000 + k, threads)
+    _, res = cpu_rate(oracle, cfg, c, t, 100, args.steps, threads)
     dt = time.perf_counter() - t0
-    value = args.steps * seq_len / dt
-    sample = f"1 sequence x L={seq_len} per step (of the {batch}-sequence per-GPU batch), all layers"
+    value = res / dt
     line = {
-        "impl": "reference", "metric": metric_name(args.config, c, batch), "value": value, "unit": UNIT,
+        "impl": "reference", "metric": metric_name(args.config, c), "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong" if c["dms"] else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded uniform residues, random-init N(0,0.02) weights)",
-        "config": {"workload": c["desc"] + f" (CPU: {seq_len}-token sequences)", "seq_len": seq_len},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "config": {"workload": c["desc"], "cpu_sample": cpu_sample_desc(c, cfg)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": cpu_sample_desc(c, cfg)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def timed_loop(step, steps, stream, dev, world, dist):
+    """Runs `steps` steps between a barrier + synchronize on both sides; CUDA events on the
+    launching stream; max over ranks (ms)."""
+    import torch
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def max_over_ranks(x, dev, world, dist):
+    import torch
+    if world == 1:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class PackedBatch:
+    """A batch on the device in the packed layout, with a gather buffer of `rows_max` rows per rank
+    for the outputs that cross between GPUs."""
+
+    def __init__(self, torch, dev, seqs, vocab, contacts, world, rows_max):
+        self.seqs = seqs
+        self.lengths = np.array([len(q) for q in seqs], dtype=np.int32)
+        self.T = int(self.lengths.sum())
+        self.cu = np.concatenate([[0], np.cumsum(self.lengths)]).astype(np.int32)
+        self.tokens = torch.from_numpy(np.concatenate(seqs).astype(np.int32)).to(dev) if seqs else None
+        self.logits = torch.zeros(max(self.T, rows_max, 1), vocab, device=dev)
+        n_map = int(sum(max(int(L) - 2, 0) ** 2 for L in self.lengths))
+        self.contacts = torch.empty(max(n_map, 1), device=dev) if contacts else None
+        self.rows_max = rows_max
+        self.gathered = torch.empty(world * rows_max, vocab, device=dev) if world > 1 else None
 
 
 def run_ours(args):
@@ -205,40 +263,54 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
     c = CONFIGS[args.config]
-    arch, dtype, seq_len = c["arch"], c["dtype"], c["seq_len"]
-    batch = args.batch or c["batch"]  # a smaller per-GPU batch is for profiler captures only
+    arch, dtype = c["arch"], c["dtype"]
+    batch = args.batch or c["batch"]  # a smaller batch is for profiler captures only
     cfg = esm.EsmConfig.preset(arch)
-    t32 = esm.synth_fp32_tensors(cfg, seed=0)
+    t32 = esm.synth_fp32_tensors(cfg, seed=synth.WEIGHT_SEED)
     tensors = esm.quantize_tensors(t32, dtype)
     del t32
     model = esm.Model(local)
     model.load_tensors(cfg, dtype, tensors)
     if c["contacts"]:
-        cw = (np.random.default_rng(7).standard_normal(cfg.n_layers * cfg.n_heads) * 0.1).astype(np.float32)
-        model.set_contact_head(cw, 0.0)
-    seqs = workload_sequences(esm, c, batch, rank)
-    lengths = np.array([len(q) for q in seqs], dtype=np.int32)
-    T = int(lengths.sum())
-    Lmax = int(lengths.max())
-    model.reserve(T, batch, Lmax, contacts=c["contacts"])
-    host_tokens = np.zeros((batch, Lmax), dtype=np.int32)
-    for i, q in enumerate(seqs):
-        host_tokens[i, : len(q)] = q
-    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
-    d_tokens = torch.from_numpy(np.concatenate(seqs).astype(np.int32)).to(dev)
-    d_logits = torch.empty(T, cfg.vocab_size, device=dev)
-    n_map = int(sum(max(int(L) - 2, 0) ** 2 for L in lengths))
-    d_contacts = torch.empty(max(n_map, 1), device=dev) if c["contacts"] else None
-    gathered = torch.empty(world * T, cfg.vocab_size, device=dev) if world > 1 else None
+        model.set_contact_head(synth.contact_head(cfg), 0.0)
+    V = cfg.vocab_size
+
+    if c["dms"]:
+        # Strong scaling of the scan: this rank's contiguous block of the masked variants.
+        lens_all = [c["seq_len"]] * batch
+        blocks = esm.partition(lens_all, world, cfg.dim, cfg.hidden_dim)
+        mine = blocks[rank]
+        seqs = synth.workload_sequences(c, len(mine), first=mine.start) if len(mine) else []
+        scaling = "strong"
+        total_tokens = batch * c["seq_len"]
+        rows_max = max(len(b) for b in blocks)  # one masked row per variant crosses between GPUs
+    else:
+        seqs = synth.workload_sequences(c, batch, seed_offset=rank)
+        scaling = "weak"
+        total_tokens = None
+        rows_max = sum(len(q) for q in seqs)
+    pb = PackedBatch(torch, dev, seqs, V, c["contacts"], world, rows_max)
+    Lmax = int(pb.lengths.max()) if len(seqs) else c["seq_len"]
+    model.reserve(max(pb.T, c["seq_len"]), max(len(seqs), 1), Lmax, contacts=c["contacts"])
+    if c["dms"]:
+        mask_rows = torch.from_numpy((pb.cu[:-1] + 1 + (np.arange(len(seqs)) + mine.start) % (c["seq_len"] - 2))
+                                     .astype(np.int64)).to(dev)
+        sel = torch.zeros(rows_max, V, device=dev)
     # A dedicated stream: the forward is enqueued on it and the CUDA events are recorded on it.
     # (torch's default stream has handle 0, which the C ABI reads as "the context's own stream".)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
 
     def step():
-        model.forward_device(d_tokens, cu, d_logits, d_contacts=d_contacts, stream=stream)
+        if pb.T:
+            model.forward_device(pb.tokens, pb.cu, pb.logits, d_contacts=pb.contacts, stream=stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, d_logits)
+            if c["dms"]:
+                if pb.T:
+                    sel[: len(seqs)] = pb.logits.index_select(0, mask_rows)
+                dist.all_gather_into_tensor(pb.gathered, sel)
+            else:
+                dist.all_gather_into_tensor(pb.gathered, pb.logits[: pb.rows_max])
 
     for _ in range(args.warmup):
         step()
@@ -248,68 +320,91 @@ def run_ours(args):
     sampler = ClockSampler([physical_gpu(local)] if physical_gpu(local) is not None else None)
     sampler.start()
     time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    ms = timed_loop(step, args.steps, stream, dev, world, dist)
     clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
     model.check_device()
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * T * args.steps / (ms / 1000.0)
     if ms <= 0.0:
         raise SystemExit("timed region is empty: the forward did not run on the timed stream")
+    if total_tokens is None:  # weak scaling: the tokens of every rank's own batch
+        total_tokens = pb.T
+        if world > 1:
+            tt = torch.tensor([pb.T], device=dev, dtype=torch.int64)
+            dist.all_reduce(tt)
+            total_tokens = int(tt.item())
+    value = total_tokens * args.steps / (ms / 1000.0)
 
-    # End to end through the host API: pinned host tokens in, results back to host every step.
-    host_tok = torch.from_numpy(host_tokens).pin_memory()
-    host_logits = torch.empty(batch, Lmax, cfg.vocab_size, dtype=torch.float32).pin_memory()
-    tok_np, log_np = host_tok.numpy(), host_logits.numpy()
-    host_con, con_np = None, None
-    if c["contacts"]:
-        np_ = max(Lmax - 2, 0)
-        host_con = torch.empty(batch, np_, np_, dtype=torch.float32).pin_memory()
-        con_np = host_con.numpy()
-    d2h = batch * Lmax * cfg.vocab_size * 4 + (batch * max(Lmax - 2, 0) ** 2 * 4 if c["contacts"] else 0)
+    # Strong scaling of the headline batch (N > 1): the one batch split across the ranks.
+    strong = None
+    if world > 1 and not c["dms"]:
+        all_seqs = synth.workload_sequences(c, batch, seed_offset=0)
+        parts = esm.partition([len(q) for q in all_seqs], world, cfg.dim, cfg.hidden_dim)
+        rows = [sum(len(all_seqs[i]) for i in p) for p in parts]
+        sb = PackedBatch(torch, dev, [all_seqs[i] for i in parts[rank]], V, c["contacts"], world, max(rows))
 
-    def e2e_step():
-        model.forward(tok_np, lengths=lengths, logits_out=log_np, want_contacts=c["contacts"], contacts_out=con_np)
+        def sstep():
+            if sb.T:
+                model.forward_device(sb.tokens, sb.cu, sb.logits, d_contacts=sb.contacts, stream=stream)
+            dist.all_gather_into_tensor(sb.gathered, sb.logits[: sb.rows_max])
 
+        for _ in range(args.warmup):
+            sstep()
+        torch.cuda.synchronize(dev)
+        sms = timed_loop(sstep, args.steps, stream, dev, world, dist)
+        tot = sum(rows)
+        strong = {"value": tot * args.steps / (sms / 1000.0), "unit": UNIT, "ms_per_step": sms / args.steps,
+                  "sequences_total": len(all_seqs), "tokens_total": tot,
+                  "sequences_per_gpu": [len(p) for p in parts], "scaling": "strong",
+                  "collective": "NCCL all_gather of the logits after each forward"}
+        del sb
+        model.check_device()
+
+    # End to end through the host API: host buffers in, results back to host every step.
     e2e_steps = max(1, min(args.steps, 5))
+    if c["dms"]:
+        wt = synth.dms_wildtype(c["seq_len"])
+        scores = torch.zeros(rows_max, 21, device=dev)
+        gathered_scores = torch.empty(world * rows_max, 21, device=dev) if world > 1 else None
+
+        def e2e_step():
+            if len(mine):
+                d, e = model.dms_masked_marginal_range(wt, mine.start, mine.stop)
+                scores[: len(mine), :20] = torch.from_numpy(d)
+                scores[: len(mine), 20] = torch.from_numpy(e)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered_scores, scores)
+                gathered_scores.cpu()
+        h2d = int(wt.nbytes)
+        d2h = int(len(mine) * 21 * 4 * (world if world > 1 else 1))
+    else:
+        host_tokens = np.zeros((len(seqs), Lmax), dtype=np.int32)
+        for i, q in enumerate(seqs):
+            host_tokens[i, : len(q)] = q
+        host_tok = torch.from_numpy(host_tokens).pin_memory()
+        host_logits = torch.empty(len(seqs), Lmax, V, dtype=torch.float32).pin_memory()
+        tok_np, log_np = host_tok.numpy(), host_logits.numpy()
+        con_np = None
+        if c["contacts"]:
+            np_ = max(Lmax - 2, 0)
+            con_np = torch.empty(len(seqs), np_, np_, dtype=torch.float32).pin_memory().numpy()
+
+        def e2e_step():
+            model.forward(tok_np, lengths=pb.lengths, logits_out=log_np, want_contacts=c["contacts"],
+                          contacts_out=con_np)
+        h2d = int(host_tokens.nbytes + 4 * len(seqs))
+        d2h = len(seqs) * Lmax * V * 4 + (len(seqs) * max(Lmax - 2, 0) ** 2 * 4 if c["contacts"] else 0)
     e2e_step()
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         e2e_step()
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_value = world * T * e2e_steps / e2e_s
-    dms_rate = None
-    if c["dms"]:
-        # The public mutational-scan call on the same wild type: masked variants built, run and
-        # scored inside the library, scores [n, 20] back to host.
-        residues = esm.random_sequences(1, c["seq_len"], seed=2000)[0][1:-1]  # the wild type
-        model.dms_masked_marginal(residues)
-        t0 = time.perf_counter()
-        model.dms_masked_marginal(residues)
-        dms_rate = len(residues) / (time.perf_counter() - t0)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, dev, world, dist)
+    e2e_value = total_tokens * e2e_steps / e2e_s
 
     # Per-kernel-class device time of one step (CUDA events around each launch, its own stream).
     model.profile_enable(True)
-    model.forward_device(d_tokens, cu, d_logits, d_contacts=d_contacts, stream=stream)
+    if pb.T:
+        model.forward_device(pb.tokens, pb.cu, pb.logits, d_contacts=pb.contacts, stream=stream)
     torch.cuda.synchronize(dev)
     prof = model.profile_read()
     model.profile_enable(False)
@@ -320,16 +415,17 @@ def run_ours(args):
     gemm_tflops = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
     traffic = None
     tp = ROOT / "profiles" / "gemm_tc_650m_q4_traffic.txt"
-    if tp.exists():
+    if tp.exists() and args.config == "c4":
         for ln in tp.read_text().splitlines():
             if ln.startswith("dram_bytes_per_launch:"):
                 traffic = float(ln.split(":", 1)[1])
+    tot_ms = sum(v["ms"] for v in prof.values())
     roofline = {
         "kernel": "gemm_tc_kernel (tcgen05 projections: QKV, O, fc1, fc2, LM dense)",
         "bound": "tensor", "achieved": gemm_tflops, "peak": sustained, "unit": "TFLOP/s",
         "frac": gemm_tflops / sustained if sustained else None, "traffic": traffic,
         "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside the step)",
-        "step_share": g["ms"] / sum(v["ms"] for v in prof.values()),
+        "step_share": g["ms"] / tot_ms if tot_ms > 0 else None,
     }
     breakdown = {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
                      "tflops": round(v["flops"] / (v["ms"] / 1000) / 1e12, 1) if v["ms"] > 0 and v["flops"] else None,
@@ -339,35 +435,41 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = oracle_module()
+        ccfg, ct = cpu_weights(oracle, c)
         threads = os.cpu_count() or 1
-        rate = cpu_forward_rate(cfg, dtype, tensors, seq_len, 4242, threads)
-        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"1 sequence x L={seq_len}, full {cfg.n_layers}-layer forward "
-                         "(CPU restatement of the reference)"}
+        rate, _ = cpu_rate(oracle, ccfg, c, ct, 100, 1, threads)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": cpu_sample_desc(c, ccfg)}
 
     if rank == 0:
+        cfg_desc = {"workload": c["desc"] + (" per GPU" if scaling == "weak" else ""),
+                    "batch_per_gpu": len(seqs), "seq_len": Lmax, "tokens_per_gpu": pb.T,
+                    "arithmetic": "f16 tensor-core operands, f32 accumulate; "
+                                  + ["FP32", "Q8_0", "Q4_0"][dtype] + " weights dequantised per layer",
+                    "parallelism": (f"variant-sharded x{world} (contiguous blocks), masked-row all-gather" if c["dms"]
+                                    else f"sequence-sharded x{world}, logits all-gather"),
+                    "scaling_of_value": scaling,
+                    "l2": "no flush: the per-step working set (activations, weights) exceeds the 126 MB L2"}
         line = {
-            "metric": metric_name(args.config, c, batch), "value": value, "unit": UNIT, "n_gpus": world,
+            "metric": metric_name(args.config, c), "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": scaling, "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (seeded uniform residues, random-init N(0,0.02) weights)",
-            "config": {"workload": c["desc"], "batch_per_gpu": batch, "seq_len": Lmax, "tokens_per_gpu": T,
-                       "arithmetic": "f16 tensor-core operands, f32 accumulate; "
-                                     + ["FP32", "Q8_0", "Q4_0"][dtype] + " weights dequantised per layer",
-                       "parallelism": f"sequence-sharded x{world}, logits all-gather",
-                       "l2": "no flush: the per-step working set (activations, weights) exceeds the 126 MB L2"},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(host_tokens.nbytes + 4 * batch),
-                    "d2h_bytes_per_step": int(d2h), "steps": e2e_steps},
+            "config": cfg_desc,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(d2h),
+                    "steps": e2e_steps},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roofline,
-            "achieved_model_tflops": total_flops / (ms / args.steps / 1000.0) / 1e12,
+            "achieved_model_tflops": total_flops / (ms / args.steps / 1000.0) / 1e12 if pb.T else None,
             "kernel_breakdown_ms_per_step": breakdown,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
-        if dms_rate is not None:
-            line["dms_variants_per_s"] = dms_rate
+        if strong is not None:
+            line["strong_scaling"] = strong
+        if c["dms"]:
+            line["dms_variants_per_s"] = batch * e2e_steps / e2e_s
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:

@@ -1493,10 +1493,15 @@ int esm_dms_wildtype_marginal(esm_ctx* c, const int32_t* residues, int32_t n, in
   return check_device_word(c);
 }
 
-int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
-                            float* entropy) {
+namespace {
+
+// Masked-marginal rows of positions [pb, pe) of the n-residue sequence into deltas[(pe - pb), 20]
+// and entropy[pe - pb] (host).
+int dms_masked_impl(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, int32_t pb, int32_t pe,
+                    float* deltas, float* entropy) {
   if (!c || !residues || !deltas || !entropy) return fail(c, ESM_EINVAL, "null argument");
   if (n <= 0) return fail(c, ESM_EINVAL, "Sequence cannot be empty");
+  if (pb < 0 || pe > n || pb >= pe) return fail(c, ESM_EINVAL, "position range must satisfy 0 <= begin < end <= n");
   std::lock_guard<std::mutex> lk(c->mu);
   if (!c->loaded) return fail(c, ESM_EINVAL, "no weights loaded");
   for (int32_t i = 0; i < n; ++i)  // the wild-type ids index the logits rows
@@ -1511,8 +1516,9 @@ int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int3
   if (actual_window + 2 > c->cap_len)
     return fail(c, ESM_ECAPACITY, "window of " + std::to_string(actual_window + 2) + " tokens exceeds max_len " +
                                       std::to_string(c->cap_len));
-  // Staging: tok_row[n] | wt_tok[n] | deltas[20 n] | entropy[n]
-  const size_t need = static_cast<size_t>(n) * (2 * 4 + 21 * 4);
+  // Staging: tok_row[m] | wt_tok[m] | deltas[20 m] | entropy[m] for the m = pe - pb positions.
+  const int m = pe - pb;
+  const size_t need = static_cast<size_t>(m) * (2 * 4 + 21 * 4);
   if (need > c->dms_cap) {
     if (c->d_dms) cudaFree(c->d_dms);
     c->d_dms = nullptr;
@@ -1521,13 +1527,13 @@ int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int3
     c->dms_cap = need;
   }
   int32_t* d_row = static_cast<int32_t*>(c->d_dms);
-  int32_t* d_wt = d_row + n;
-  float* d_delta = reinterpret_cast<float*>(d_wt + n);
-  float* d_ent = d_delta + static_cast<size_t>(20) * n;
+  int32_t* d_wt = d_row + m;
+  float* d_delta = reinterpret_cast<float*>(d_wt + m);
+  float* d_ent = d_delta + static_cast<size_t>(20) * m;
   std::vector<int32_t> toks, cu{0}, rows, wts;
-  int p0 = 0;
-  for (int p = 0; p <= n; ++p) {
-    const bool flush = (p == n) || static_cast<int>(cu.size()) - 1 == c->cap_seqs ||
+  int p0 = 0;  // first position of the current batch, relative to pb
+  for (int p = pb; p <= pe; ++p) {
+    const bool flush = (p == pe) || static_cast<int>(cu.size()) - 1 == c->cap_seqs ||
                        cu.back() + actual_window + 2 > c->cap_tokens;
     if (flush && cu.size() > 1) {
       // One batch of masked variants through the forward, then score their masked rows.
@@ -1547,9 +1553,9 @@ int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int3
       rows.clear();
       wts.clear();
       cu.assign(1, 0);
-      p0 = p;
+      p0 = p - pb;
     }
-    if (p == n) break;
+    if (p == pe) break;
     int w_start;
     if (p < half_w) w_start = 0;
     else if (p + half_w > n) w_start = std::max(n - actual_window, 0);
@@ -1565,10 +1571,22 @@ int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int3
     wts.push_back(residues[p]);
     cu.push_back(base + (w_end - w_start) + 2);
   }
-  ESM_CUDA(cudaMemcpyAsync(deltas, d_delta, static_cast<size_t>(20) * n * 4, cudaMemcpyDeviceToHost, s));
-  ESM_CUDA(cudaMemcpyAsync(entropy, d_ent, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, s));
+  ESM_CUDA(cudaMemcpyAsync(deltas, d_delta, static_cast<size_t>(20) * m * 4, cudaMemcpyDeviceToHost, s));
+  ESM_CUDA(cudaMemcpyAsync(entropy, d_ent, static_cast<size_t>(m) * 4, cudaMemcpyDeviceToHost, s));
   ESM_CUDA(cudaStreamSynchronize(s));
   return check_device_word(c);
+}
+
+}  // namespace
+
+int esm_dms_masked_marginal(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
+                            float* entropy) {
+  return dms_masked_impl(c, residues, n, window_size, 0, n, deltas, entropy);
+}
+
+int esm_dms_masked_marginal_range(esm_ctx* c, const int32_t* residues, int32_t n, int32_t window_size,
+                                  int32_t pos_begin, int32_t pos_end, float* deltas, float* entropy) {
+  return dms_masked_impl(c, residues, n, window_size, pos_begin, pos_end, deltas, entropy);
 }
 
 int esm_matmul_tiled(esm_ctx* c, int32_t dtype, const float* x, const void* w, const float* bias, int32_t in_dim,

@@ -15,10 +15,12 @@
 //   * Its device address is obtained once per device with cudaGetSymbolAddress (host code cannot
 //     use the symbol itself). The first call on a device does that set-up and also loads the
 //     kernels it uses, so that first call should come before any stream capture.
-//   * Every call shares the array and it keeps the previous call's contents: this entry point
-//     clears what must start at zero (the padded bias) on every call. Calls that overlap on the
-//     GPU (different streams, host threads or devices sharing one process) race on the array and
-//     must be serialised by the caller.
+//   * Every call on a device shares that device's array and it keeps the previous call's contents:
+//     this entry point clears what must start at zero (the padded bias) on every call. Calls that
+//     overlap on the same device (different streams or host threads) race on the array and must be
+//     serialised by the caller; calls on different devices use each device's own copy.
+//   * The stream and the buffers must belong to the calling thread's current device, whose array
+//     the call uses; a stream or output buffer of another device is refused (ESM_EINVAL).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -77,12 +79,13 @@ size_t round256(size_t n) { return (n + 255) / 256 * 256; }
 extern "C" int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const void* d_w, const float* d_bias,
                                         int32_t in_dim, int32_t out_dim, int32_t seq_len, float* d_out,
                                         void* stream) {
-  if (dtype < ESM_DTYPE_FP32 || dtype > ESM_DTYPE_Q4_0) return ESM_EINVAL;
+  if (dtype < ESM_DTYPE_FP32 || dtype > ESM_DTYPE_Q3_LUT) return ESM_EINVAL;
   if (!d_x || !d_w || !d_out || in_dim <= 0 || in_dim % 32 || out_dim <= 0 || seq_len <= 0) return ESM_EINVAL;
-  // Vector loads and stores need 16-byte aligned fp32 operands; blocks need 4-byte alignment.
+  // Vector loads and stores need 16-byte aligned fp32 operands; Q8_0 / Q4_0 blocks are read as
+  // 32-bit words, Q3_LUT blocks byte by byte.
+  const uintptr_t w_align = dtype == ESM_DTYPE_FP32 ? 15 : (dtype == ESM_DTYPE_Q3_LUT ? 0 : 3);
   if ((reinterpret_cast<uintptr_t>(d_x) & 15) || (reinterpret_cast<uintptr_t>(d_out) & 15) ||
-      (reinterpret_cast<uintptr_t>(d_w) & (dtype == ESM_DTYPE_FP32 ? 15 : 3)) ||
-      (reinterpret_cast<uintptr_t>(d_bias) & 3))
+      (reinterpret_cast<uintptr_t>(d_w) & w_align) || (reinterpret_cast<uintptr_t>(d_bias) & 3))
     return ESM_EINVAL;
   const int n_pad = (out_dim + 15) / 16 * 16;
   const int bn = esm::gemm_pick_bn_any(n_pad);
@@ -97,6 +100,17 @@ extern "C" int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const v
   int rc = device_slot(&slot);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array used is the current device's: the stream and the output must be on that device.
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return ESM_ECUDA;
+  if (s) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(s, &sdev) != cudaSuccess) return ESM_EINVAL;
+    if (sdev != cur) return ESM_EINVAL;
+  }
+  cudaPointerAttributes pa{};
+  if (cudaPointerGetAttributes(&pa, d_out) != cudaSuccess) return ESM_EINVAL;
+  if (pa.type == cudaMemoryTypeDevice && pa.device != cur) return ESM_EINVAL;
   __half* x16 = reinterpret_cast<__half*>(slot->scratch);
   __half* w16 = reinterpret_cast<__half*>(slot->scratch + x16_bytes);
   float* bias = reinterpret_cast<float*>(slot->scratch + x16_bytes + w16_bytes);
@@ -129,9 +143,11 @@ extern "C" int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const v
   if (e == cudaSuccess && padded_out)
     e = cudaMemcpy2DAsync(d_out, static_cast<size_t>(out_dim) * 4, out, static_cast<size_t>(n_pad) * 4,
                           static_cast<size_t>(out_dim) * 4, seq_len, cudaMemcpyDeviceToDevice, s);
+  // The error word comes back on the call's own stream (no legacy-default-stream copy, which
+  // would wait for every blocking stream of the device).
+  int h_err = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&h_err, slot->err, sizeof(int), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return ESM_ECUDA;
-  int h_err = 0;
-  if (cudaMemcpy(&h_err, slot->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return ESM_ECUDA;
   return h_err ? ESM_ETIMEOUT : ESM_OK;
 }

@@ -14,6 +14,8 @@ from pathlib import Path
 
 import numpy as np
 
+from synth import random_sequences, synth_fp32_tensors  # noqa: F401 (re-exported)
+
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libesm_b200.so"
 
@@ -119,6 +121,18 @@ def lib() -> ctypes.CDLL:
             "esm_matmul_tiled": [vp, i32, vp, vp, vp, i32, i32, i32, vp],
             "esm_dms_masked_marginal": [vp, vp, i32, i32, vp, vp],
             "esm_dms_wildtype_marginal": [vp, vp, i32, i32, i32, vp, vp],
+            "esm_dms_masked_marginal_range": [vp, vp, i32, i32, i32, i32, vp, vp],
+            "esm_partition": [vp, i32, i32, i32, i32, vp],
+            "esm_group_create": [vp, i32, vp],
+            "esm_group_destroy": [vp],
+            "esm_group_size": [vp, vp],
+            "esm_group_ctx": [vp, i32, vp],
+            "esm_group_load_host": [vp, vp, i32, vp, vp],
+            "esm_group_load_file": [vp, ctypes.c_char_p, vp],
+            "esm_group_set_contact_head": [vp, vp, i32, f32],
+            "esm_group_reserve": [vp, i32, i32, i32, i32],
+            "esm_group_forward": [vp, vp, vp, i32, i32, vp, vp, vp],
+            "esm_group_dms_masked_marginal": [vp, vp, i32, i32, vp, vp],
             "esm_check_device": [vp],
             "esm_probe_wait_timeout": [vp, i32],
             "esm_profile_enable": [vp, i32],
@@ -130,6 +144,8 @@ def lib() -> ctypes.CDLL:
             fn.restype = ctypes.c_int
         L.esm_last_error.argtypes = [vp]
         L.esm_last_error.restype = ctypes.c_char_p
+        L.esm_group_last_error.argtypes = [vp]
+        L.esm_group_last_error.restype = ctypes.c_char_p
         _lib = L
     return _lib
 
@@ -195,53 +211,6 @@ def detect_file(path: str) -> tuple[EsmConfig, int]:
 
 # ---- synthetic weights ---------------------------------------------------------------------------
 
-def synth_fp32_tensors(cfg: EsmConfig, seed: int = 0, std: float = 0.02, bias_std: float = 0.0,
-                       ln_jitter: float = 0.0, tie_decoder: bool = True, with_classifier: bool = True) -> dict:
-    """Seeded random-init ESM-2 weights in EsmWeights order (float32 numpy arrays).
-
-    Matrices and the embedding ~ N(0, std); biases ~ N(0, bias_std) (0 by default); LayerNorm
-    gamma = 1 + N(0, ln_jitter), beta = N(0, ln_jitter). The classifier is
-    [lm_ln_w | lm_ln_b | dense_w | dense_b | dec_w | dec_b] with dec_w a copy of the embedding
-    when tie_decoder (the ESM-2 LM head is tied to the token embedding).
-    """
-    rng = np.random.default_rng(seed)
-    d, F, nl, V = cfg.dim, cfg.hidden_dim, cfg.n_layers, cfg.vocab_size
-
-    def normal(n, s):
-        if s == 0.0:
-            return np.zeros(n, dtype=np.float32)
-        a = rng.standard_normal(n, dtype=np.float32)
-        a *= np.float32(s)
-        return a
-
-    def gamma(n):
-        return (np.ones(n, dtype=np.float32) + normal(n, ln_jitter)).astype(np.float32)
-
-    t = {}
-    t["tok_emb"] = normal(V * d, std)
-    t["ln1_w"] = gamma(nl * d)
-    t["ln1_b"] = normal(nl * d, ln_jitter)
-    for w, b in (("wq", "bq"), ("wk", "bk"), ("wv", "bv"), ("wo", "bo")):
-        t[w] = normal(nl * d * d, std)
-        t[b] = normal(nl * d, bias_std)
-    t["ln2_w"] = gamma(nl * d)
-    t["ln2_b"] = normal(nl * d, ln_jitter)
-    t["fc1_w"] = normal(nl * F * d, std)
-    t["fc1_b"] = normal(nl * F, bias_std)
-    t["fc2_w"] = normal(nl * d * F, std)
-    t["fc2_b"] = normal(nl * d, bias_std)
-    t["lnf_w"] = gamma(d)
-    t["lnf_b"] = normal(d, ln_jitter)
-    if with_classifier:
-        dec_w = t["tok_emb"].copy() if tie_decoder else normal(V * d, std)
-        t["classifier"] = np.concatenate([
-            gamma(d), normal(d, ln_jitter), normal(d * d, std), normal(d, bias_std), dec_w, normal(V, bias_std),
-        ]).astype(np.float32)
-    else:
-        t["classifier"] = np.zeros(0, dtype=np.float32)
-    return t
-
-
 def quantize_tensors(t: dict, dtype: int) -> dict:
     """Applies EsmWeights::quantize_q8 / quantize_q4 (src/lib.rs:558-607): the six matrices become
     blocks; for Q8_0 the token embedding is quantized too, for Q4_0 it stays FP32."""
@@ -258,19 +227,6 @@ def quantize_tensors(t: dict, dtype: int) -> dict:
         out[m] = q(t[m])
     if dtype == DTYPE_Q8_0:
         out["tok_emb"] = quantize_q8(t["tok_emb"])
-    return out
-
-
-def random_sequences(n: int, lengths, seed: int = 0) -> list[np.ndarray]:
-    """Token sequences <cls> + residues uniform over the 20 canonical ids 4..23 + <eos>."""
-    rng = np.random.default_rng(seed)
-    lens = [lengths] * n if np.isscalar(lengths) else list(lengths)
-    out = []
-    for L in lens:
-        s = np.empty(L, dtype=np.int32)
-        s[0], s[-1] = 0, 2
-        s[1:-1] = rng.integers(4, 24, size=L - 2, dtype=np.int32)
-        out.append(s)
     return out
 
 
@@ -486,6 +442,17 @@ class Model:
                   "esm_dms_masked_marginal")
         return deltas, ent
 
+    def dms_masked_marginal_range(self, residues, pos_begin: int, pos_end: int, window_size: int = 0):
+        """Rows [pos_begin, pos_end) of dms_masked_marginal on the same sequence (the block of a
+        scan one GPU runs when the scan is split across GPUs)."""
+        r = np.ascontiguousarray(residues, dtype=np.int32)
+        m = pos_end - pos_begin
+        deltas = np.empty((max(m, 0), 20), dtype=np.float32)
+        ent = np.empty(max(m, 0), dtype=np.float32)
+        self._chk(lib().esm_dms_masked_marginal_range(self._ctx, _p(r), r.size, window_size, pos_begin, pos_end,
+                                                      _p(deltas), _p(ent)), "esm_dms_masked_marginal_range")
+        return deltas, ent
+
     def matmul_tiled(self, dtype: int, x, w, bias, in_dim: int, out_dim: int) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32)
         seq_len = x.size // in_dim
@@ -515,3 +482,84 @@ class Model:
 
     def check_device(self) -> None:
         self._chk(lib().esm_check_device(self._ctx), "esm_check_device")
+
+
+# ---- several GPUs from one process -------------------------------------------------------------
+
+def partition(lengths, parts: int, dim: int, hidden_dim: int) -> list[range]:
+    """esm_partition: contiguous cost-balanced blocks of sequence indices, one per device."""
+    ln = np.ascontiguousarray(lengths, dtype=np.int32)
+    bounds = np.zeros(parts + 1, dtype=np.int32)
+    _check(lib().esm_partition(_p(ln), ln.size, dim, hidden_dim, parts, _p(bounds)), "esm_partition")
+    return [range(int(bounds[r]), int(bounds[r + 1])) for r in range(parts)]
+
+
+class Group:
+    """esm_group: one context per device of one host process, with the batch split across them."""
+
+    def __init__(self, devices):
+        devs = np.ascontiguousarray(devices, dtype=np.int32)
+        self._g = ctypes.c_void_p()
+        rc = lib().esm_group_create(_p(devs), devs.size, ctypes.byref(self._g))
+        if rc != ESM_OK:
+            raise EsmError(rc, f"esm_group_create(devices={list(devices)}) failed")
+        self.devices = [int(d) for d in devs]
+        self.cfg: EsmConfig | None = None
+
+    def close(self) -> None:
+        if self._g:
+            lib().esm_group_destroy(self._g)
+            self._g = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _chk(self, rc: int, what: str) -> None:
+        if rc != ESM_OK:
+            raise EsmError(rc, f"{what}: {lib().esm_group_last_error(self._g).decode()}")
+
+    def load_tensors(self, cfg: EsmConfig, dtype: int, tensors: dict) -> None:
+        arrs = [np.ascontiguousarray(tensors[n]) for n in TENSOR_NAMES]
+        ptrs = (ctypes.c_void_p * 20)(*[a.ctypes.data if a.size else None for a in arrs])
+        sizes = (ctypes.c_size_t * 20)(*[a.nbytes for a in arrs])
+        c = cfg.c_struct()
+        self._chk(lib().esm_group_load_host(self._g, ctypes.byref(c), dtype, ptrs, sizes), "esm_group_load_host")
+        self.cfg = cfg
+
+    def set_contact_head(self, w, b: float) -> None:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        self._chk(lib().esm_group_set_contact_head(self._g, _p(w), w.size, float(b)), "esm_group_set_contact_head")
+
+    def reserve(self, max_tokens: int, max_seqs: int, max_len: int, contacts: bool = False) -> None:
+        self._chk(lib().esm_group_reserve(self._g, max_tokens, max_seqs, max_len, int(contacts)), "esm_group_reserve")
+
+    def forward(self, seqs, want_hidden: bool = False, want_contacts: bool = False) -> dict:
+        lengths = np.array([len(s) for s in seqs], dtype=np.int32)
+        B, Lmax = len(seqs), int(lengths.max())
+        tokens = np.zeros((B, Lmax), dtype=np.int32)
+        for i, s in enumerate(seqs):
+            tokens[i, : len(s)] = s
+        cfg = self.cfg
+        logits = np.empty((B, Lmax, cfg.vocab_size), dtype=np.float32)
+        hidden = np.empty((B, Lmax, cfg.dim), dtype=np.float32) if want_hidden else None
+        np_ = max(Lmax - 2, 0)
+        contacts = np.empty((B, np_, np_), dtype=np.float32) if want_contacts else None
+        self._chk(lib().esm_group_forward(self._g, _p(tokens), _p(lengths), B, Lmax, _p(logits), _p(hidden),
+                                          _p(contacts)), "esm_group_forward")
+        res = {"logits": logits, "lengths": lengths}
+        if want_hidden:
+            res["hidden"] = hidden
+        if want_contacts:
+            res["contacts"] = contacts
+        return res
+
+    def dms_masked_marginal(self, residues, window_size: int = 0):
+        r = np.ascontiguousarray(residues, dtype=np.int32)
+        deltas = np.empty((r.size, 20), dtype=np.float32)
+        ent = np.empty(r.size, dtype=np.float32)
+        self._chk(lib().esm_group_dms_masked_marginal(self._g, _p(r), r.size, window_size, _p(deltas), _p(ent)),
+                  "esm_group_dms_masked_marginal")
+        return deltas, ent

@@ -3,7 +3,7 @@
  *
  * Drop-in for the hot path of codon-infer v1.12.0 (Rust crate, src/lib.rs): the
  * forward_bidirectional* family, its weight formats and its outputs. Plain C types only, so the
- * Rust host binds it with an `extern "C"` block (see INTEGRATION.md). Every function returns an
+ * Rust host binds it with an `extern "C"` block. Every function returns an
  * ESM_* status code and never aborts; esm_last_error() gives the message of the last failure on a
  * context.
  *
@@ -203,6 +203,13 @@ int esm_forward_device(esm_ctx* ctx, const int32_t* d_tokens, const int32_t* h_c
 int esm_dms_masked_marginal(esm_ctx* ctx, const int32_t* residues, int32_t n, int32_t window_size, float* deltas,
                             float* entropy);
 
+/* The rows p in [pos_begin, pos_end) of esm_dms_masked_marginal on the same n-residue sequence
+ * (same windows, same values): deltas [pos_end - pos_begin, 20] and entropy [pos_end - pos_begin],
+ * HOST buffers. This is the per-position loop body of src/pipeline.rs:111-174 over a contiguous
+ * block of positions: the unit by which a scan is split across GPUs. */
+int esm_dms_masked_marginal_range(esm_ctx* ctx, const int32_t* residues, int32_t n, int32_t window_size,
+                                  int32_t pos_begin, int32_t pos_end, float* deltas, float* entropy);
+
 /* The same scan in wild-type-marginal mode (DmsScoringMode::WildtypeMarginal, src/pipeline.rs:176-291):
  * no masking; the whole sequence is one forward when it fits the window (window_size semantics as
  * above), otherwise windows of that size `stride` residues apart (stride in (0, window], else half a
@@ -228,14 +235,59 @@ int esm_matmul_tiled(esm_ctx* ctx, int32_t dtype, const float* x, const void* w,
  * d_bias [out_dim] or NULL. Its only scratch is a static device array of ESM_NOALLOC_SCRATCH_BYTES
  * that holds the fp16 operand copies (2*(seq_len + out_dim)*in_dim bytes, 256-byte aligned each),
  * the bias padded to a multiple of 16 and, when out_dim % 16 != 0, a padded fp32 output; larger
- * problems return ESM_ECAPACITY. The array lives on every GPU where the library's device code is
- * loaded until the process exits. The first call on a device looks up the array's device address
- * and loads the kernels it uses, so make it before any stream capture. Calls share the array:
- * calls that overlap on the GPU race and must be serialised by the caller. The call is enqueued on
- * `stream` (a cudaStream_t, NULL = legacy default) and returns once the result is in d_out. */
+ * problems return ESM_ECAPACITY. dtype may be any of the four storage types (Q3_LUT blocks need no
+ * alignment). The array lives on every GPU where the library's device code is loaded until the
+ * process exits. The first call on a device looks up the array's device address and loads the
+ * kernels it uses, so make it before any stream capture. Calls on one device share its array:
+ * calls that overlap on the same device race and must be serialised by the caller; calls on
+ * different devices use each device's own copy. The stream and buffers must belong to the
+ * calling thread's current device (otherwise ESM_EINVAL). The call is enqueued on `stream` (a
+ * cudaStream_t, NULL = legacy default) and returns once the result is in d_out. */
 #define ESM_NOALLOC_SCRATCH_BYTES (32u << 20)
 int esm_matmul_tiled_noalloc(int32_t dtype, const float* d_x, const void* d_w, const float* d_bias, int32_t in_dim,
                              int32_t out_dim, int32_t seq_len, float* d_out, void* stream);
+
+/* ---- several GPUs from one host process ------------------------------------------------------ */
+
+/* The reference runs every sequence and every masked variant of a scan as its own forward, one
+ * after another on the host (src/pipeline.rs:111-174, 427-444); these calls spread that same work
+ * over several GPUs of one box. A group holds one context per listed device, each with a full
+ * copy of the weights. A batch is split into contiguous blocks of sequences with balanced cost
+ * (esm_partition), a scan into contiguous blocks of positions; one host thread per device runs its
+ * block, and each device copies its rows straight into the caller's host arrays, so results are
+ * bit for bit those of one context and no data moves between GPUs. */
+typedef struct esm_group esm_group;
+
+/* Contiguous blocks of sequences for `parts` devices: bounds[0..parts] (parts + 1 entries,
+ * bounds[0] = 0, bounds[parts] = B); block r is [bounds[r], bounds[r+1]) and may be empty. The cost
+ * of a sequence of L tokens is one layer's algorithmic FLOPs, 2L(4 dim^2 + 2 dim hidden_dim) for
+ * the projections plus 4 L^2 dim for attention; block r ends at the first sequence whose cost
+ * prefix reaches (r + 1) / parts of the total. Host-only. */
+int esm_partition(const int32_t* lengths, int32_t B, int32_t dim, int32_t hidden_dim, int32_t parts,
+                  int32_t* bounds);
+
+/* One context per entry of devices[0..n_devices) (a device may be listed twice: two contexts on
+ * one GPU). Members are destroyed by esm_group_destroy. */
+int esm_group_create(const int32_t* devices, int32_t n_devices, esm_group** out);
+int esm_group_destroy(esm_group* group);
+const char* esm_group_last_error(const esm_group* group);
+int esm_group_size(const esm_group* group, int32_t* n);
+/* Member context i (owned by the group), for per-device calls such as esm_forward_device. */
+int esm_group_ctx(esm_group* group, int32_t i, esm_ctx** out);
+/* esm_load_host / esm_load_file / esm_set_contact_head / esm_reserve on every member (in
+ * parallel). Capacities are per device: a device runs its block in chunks that fit them. */
+int esm_group_load_host(esm_group* group, const esm_config* cfg, int32_t dtype, const void* const* tensors,
+                        const size_t* sizes);
+int esm_group_load_file(esm_group* group, const char* path, const esm_config* cfg);
+int esm_group_set_contact_head(esm_group* group, const float* w, int32_t nw, float b);
+int esm_group_reserve(esm_group* group, int32_t max_tokens, int32_t max_seqs, int32_t max_len, int32_t contacts);
+/* esm_forward over the group: same arguments and outputs (HOST buffers, [B, Lmax, ...] padded). */
+int esm_group_forward(esm_group* group, const int32_t* tokens, const int32_t* lengths, int32_t B, int32_t Lmax,
+                      float* logits, float* hidden, float* contacts);
+/* esm_dms_masked_marginal over the group: positions split into equal contiguous blocks, one per
+ * device (esm_dms_masked_marginal_range); outputs as esm_dms_masked_marginal. */
+int esm_group_dms_masked_marginal(esm_group* group, const int32_t* residues, int32_t n, int32_t window_size,
+                                  float* deltas, float* entropy);
 
 /* ---- instrumentation (no counterpart in the reference, which only times whole calls) ---------- */
 

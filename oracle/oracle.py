@@ -95,6 +95,24 @@ def quantize_q4(x) -> np.ndarray:
     return out
 
 
+def quantize_tensors(t: dict, dtype: int) -> dict:
+    """EsmWeights::quantize_q8 / quantize_q4 / quantize_q3 (src/lib.rs:558-633) with the oracle's
+    quantizers: the six matrices become blocks; Q8_0 also quantizes the token embedding (Q4_0
+    keeps it FP32); Q3_LUT stores the attention matrices as Q4_0 and fc1 / fc2 as Q3_LUT."""
+    out = dict(t)
+    if dtype == DT_FP32:
+        return out
+    mats = ("wq", "wk", "wv", "wo", "fc1_w", "fc2_w")
+    for m in mats:
+        if dtype == DT_Q3:
+            out[m] = quantize_q3(t[m]) if m in ("fc1_w", "fc2_w") else quantize_q4(t[m])
+        else:
+            out[m] = quantize_q8(t[m]) if dtype == DT_Q8 else quantize_q4(t[m])
+    if dtype == DT_Q8:
+        out["tok_emb"] = quantize_q8(t["tok_emb"])
+    return out
+
+
 def dequantize_q8(blocks: np.ndarray) -> np.ndarray:
     blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
     n = blocks.size // Q8_BLOCK_BYTES * 32
@@ -161,6 +179,25 @@ def log_softmax_canonical(logits) -> np.ndarray:
     out = np.empty(33, dtype=np.float32)
     lib().orc_log_softmax_canonical(_ptr(x), _ptr(out))
     return out
+
+
+# CANONICAL_AAS token ids in column order (src/benchmark.rs:702-707).
+CANONICAL_IDS = (5, 23, 13, 9, 18, 6, 21, 12, 15, 4, 20, 17, 14, 16, 10, 8, 11, 7, 22, 19)
+
+
+def dms_scores(logits_row, wt_tok: int) -> tuple[np.ndarray, float]:
+    """One masked-marginal row of run_pipeline_dms_with_mode (src/pipeline.rs:150-171): the
+    canonical log-softmax of the masked position's logits, the Shannon entropy over ids 4..=23
+    (f32 sum, terms with p <= 1e-12 skipped), and the 20 deltas log P(aa) - log P(wt) in
+    CANONICAL_AAS order (0 for the wild-type column)."""
+    lp = log_softmax_canonical(logits_row)
+    ent = np.float32(0.0)
+    for i in range(4, 24):
+        p = np.float32(np.exp(lp[i]))
+        if p > 1e-12:
+            ent = np.float32(ent - p * lp[i])
+    deltas = np.array([0.0 if aa == wt_tok else lp[aa] - lp[wt_tok] for aa in CANONICAL_IDS], dtype=np.float32)
+    return deltas, float(ent)
 
 
 def rope_tables(max_len: int, head_dim: int):

@@ -23,6 +23,7 @@ model (docs/benchmarks_v1.6.0.md:18), which is the bar these fixtures let the or
 """
 from __future__ import annotations
 
+import os
 import re
 import sys
 from pathlib import Path
@@ -139,4 +140,6 @@ def main(ref_root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    # The codon-infer checkout: the argument, else CODON_INFER_REF, else a sibling of this repository.
+    default = os.environ.get("CODON_INFER_REF", str(Path(__file__).resolve().parents[3] / "reference"))
+    main(Path(sys.argv[1] if len(sys.argv) > 1 else default))

@@ -121,3 +121,13 @@ def test_synthetic_weights_are_seeded(esm):
     d, V = cfg.dim, cfg.vocab_size
     dec = a["classifier"][3 * d + d * d: 3 * d + d * d + V * d]
     assert np.array_equal(dec, a["tok_emb"])  # tied LM decoder
+
+
+def test_synthetic_presets_match_the_library(esm):
+    # The numpy-only presets that the CPU baseline and the fixture generators use are the
+    # library's EsmConfig presets.
+    import synth
+    for arch in range(5):
+        a, b = synth.preset(arch), esm.EsmConfig.preset(arch)
+        assert (a.dim, a.hidden_dim, a.n_layers, a.n_heads, a.vocab_size, a.arch) == \
+               (b.dim, b.hidden_dim, b.n_layers, b.n_heads, b.vocab_size, b.arch)

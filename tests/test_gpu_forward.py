@@ -6,14 +6,25 @@ Tolerances (stated by the hot-path specification): logits max-abs error <= 2e-2 
 top-1 agreement; contact probabilities max-abs <= 1e-2. Each sequence of a padded batch is
 compared with the oracle run on that sequence alone (the key-padding mask contract).
 
-Top-1 agreement is counted on the tokens whose oracle top-1 margin exceeds twice the logit
+Top-1 agreement is asserted on the tokens whose oracle top-1 margin exceeds twice the logit
 tolerance: with every logit within 2e-2 of the oracle, two candidates closer than 4e-2 may come
-out in either order. The random-weight models of these tests have flat output distributions
-(about 12 % of tokens of a 2-layer 650M-shape model have margins below 4e-2), so counting those
-near-ties would test rounding noise rather than the kernels.
+out in either order. The random-weight models of these tests (a few layers, jittered LayerNorms
+and biases) have flat output distributions (about 12 % of tokens of a 2-layer 650M-shape model
+have margins below 4e-2), so counting those near-ties would test rounding noise rather than the
+kernels. The agreement over all tokens is recorded beside it (ESM_PARITY_LOG). At full depth with
+the benchmark's weights, and on the reference's real 8M weights, margins are large and
+tests/test_gpu_parity_bench.py asserts the unfiltered rate.
+
+Hidden states (state.x, the final LayerNorm's output, of unit scale per token) have no tolerance
+in the specification; they are held to 5e-2 max-abs, a bound of this test suite's own that
+catches a wrong row or a wrong normalisation, and their measured error is recorded.
 """
+import os
+
 import numpy as np
 import pytest
+
+from conftest import parity_record
 
 pytestmark = pytest.mark.gpu
 
@@ -38,26 +49,38 @@ def build(esm, cfg, dtype, seed=0, contact=True, bias_std=0.02, ln_jitter=0.1, w
 
 
 def compare(orc, cfg, dtype, t, seqs, out, cw=None, cb=-0.5):
-    top_ok = top_n = 0
+    top_ok = top_n = all_ok = all_n = 0
+    worst = hworst = cworst = 0.0
     for i, s in enumerate(seqs):
         L = len(s)
         ref = orc.forward(cfg, dtype, t, s, contact_w=cw, contact_b=cb, want_hidden=True)
         got = out["logits"][i, :L]
         assert np.isfinite(got).all()
         err = np.abs(got - ref["logits"]).max()
+        worst = max(worst, float(err))
         assert err <= LOGIT_TOL, f"seq {i}: logits max-abs {err:.3e}"
         srt = np.sort(ref["logits"], axis=1)
         decisive = (srt[:, -1] - srt[:, -2]) > 2 * LOGIT_TOL
-        top_ok += int((got.argmax(1) == ref["logits"].argmax(1))[decisive].sum())
+        same = got.argmax(1) == ref["logits"].argmax(1)
+        top_ok += int(same[decisive].sum())
         top_n += int(decisive.sum())
+        all_ok += int(same.sum())
+        all_n += L
         if "hidden" in out:
             herr = np.abs(out["hidden"][i, :L] - ref["hidden"]).max()
+            hworst = max(hworst, float(herr))
             assert herr <= 5e-2, f"seq {i}: hidden max-abs {herr:.3e}"
         if cw is not None and L > 2:
             cerr = np.abs(out["contacts"][i, :L - 2, :L - 2] - ref["contacts"]).max()
+            cworst = max(cworst, float(cerr))
             assert cerr <= CONTACT_TOL, f"seq {i}: contacts max-abs {cerr:.3e}"
         # Padding positions are zero.
         assert (out["logits"][i, L:] == 0).all()
+    case = os.environ.get("PYTEST_CURRENT_TEST", "forward").split(" ")[0]
+    parity_record(case, logits_max_abs=worst, top1_all=all_ok / all_n,
+                  top1_decisive=top_ok / top_n if top_n else None, decisive_share=top_n / all_n,
+                  hidden_max_abs=hworst if "hidden" in out else None,
+                  contacts_max_abs=cworst if cw is not None else None)
     assert top_n == 0 or top_ok / top_n >= TOP1_MIN, f"top-1 agreement {top_ok / top_n:.4f}"
 
 

@@ -33,15 +33,18 @@ def test_noalloc_matches_allocating_entry_point_twice(esm, orc):
     model = esm.Model(0)
     dev = torch.device("cuda:0")
     stream = torch.cuda.Stream(dev)
-    # First a larger problem, then a smaller one with a ragged output width over its leftovers.
-    cases = [(esm.DTYPE_Q4_0, 1280, 640, 300), (esm.DTYPE_Q8_0, 480, 33, 77)]
+    # First a larger problem, then a smaller one with a ragged output width over its leftovers,
+    # then Q3_LUT blocks (14 bytes, so rows start at any byte).
+    cases = [(esm.DTYPE_Q4_0, 1280, 640, 300), (esm.DTYPE_Q8_0, 480, 33, 77), (esm.DTYPE_Q3_LUT, 640, 100, 50)]
     for call, (dt, in_dim, out_dim, seq_len) in enumerate(cases):
         rng = np.random.default_rng(100 + call)
         x = rng.standard_normal(seq_len * in_dim, dtype=np.float32)
         w32 = (rng.standard_normal(out_dim * in_dim, dtype=np.float32) * 0.02).astype(np.float32)
         b = (rng.standard_normal(out_dim, dtype=np.float32) * 0.1).astype(np.float32)
-        wq = esm.quantize_q4(w32) if dt == esm.DTYPE_Q4_0 else esm.quantize_q8(w32)
-        deq = orc.dequantize_q4(wq) if dt == esm.DTYPE_Q4_0 else orc.dequantize_q8(wq)
+        quant = {esm.DTYPE_Q4_0: (esm.quantize_q4, orc.dequantize_q4), esm.DTYPE_Q8_0: (esm.quantize_q8, orc.dequantize_q8),
+                 esm.DTYPE_Q3_LUT: (esm.quantize_q3, orc.dequantize_q3)}[dt]
+        wq = quant[0](w32)
+        deq = quant[1](wq)
 
         expect = model.matmul_tiled(dt, x, wq, b, in_dim, out_dim)
 
