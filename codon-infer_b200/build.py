@@ -24,7 +24,7 @@ INCLUDE = PKG.parent / "include"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-ffp-contract=off", "-I", str(INCLUDE)]
-SOURCES = ["gemm_tc.cu", "kernels.cu", "attention.cu", "attention_tc.cu", "attention_tc2.cu", "attention_tc3.cu", "contact_tc.cu", "quantize.cu", "contact_rank.cu", "esm_api.cu", "esm_group.cpp", "formats.cpp", "noalloc.cu"]
+SOURCES = ["gemm_tc.cu", "kernels.cu", "attention.cu", "attention_tc3.cu", "contact_tc.cu", "quantize.cu", "contact_rank.cu", "esm_api.cu", "esm_group.cpp", "formats.cpp", "noalloc.cu"]
 
 
 def _needs(obj: Path, deps: list[Path]) -> bool:

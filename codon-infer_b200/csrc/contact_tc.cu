@@ -12,9 +12,11 @@
 // The tile is computed transposed: S^T = K Q^T with M = 128 keys (tensor-memory lanes, one key per
 // thread) and N = 64 queries. A thread then owns a key column of P: its column sum accumulates in
 // a register, and it keeps 32 entries of M^T for its key in registers across all heads. M is only
-// ever used as M + M^T, so storing M^T in place of M gives the same contacts. The row sums need no reduction: rows of P sum to one over all L
-// keys, so rowsum over the inner keys is 1 - P[i, 0] - P[i, L-1], which the threads owning keys 0
-// and L-1 add for every query.
+// ever used as M + M^T, so storing M^T in place of M gives the same contacts. The row sums need no
+// reduction: rows of P sum to one over all L keys, so the row sum over the inner keys is
+// 1 - P[i, 0] - P[i, L-1], which contact_rowsum_kernel adds for every inner query from two dot
+// products (keeping that term out of this kernel keeps the tiles that hold key 0 or L-1 as fast as
+// the others).
 //
 // One CTA per (sequence, 128-key tile, 64-query tile); 320 threads; two CTAs per SM.
 //   warp 0      TMA producer: the K and Q tiles of each contributing head into a 4-stage ring.
@@ -212,33 +214,23 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
     const int kr = quarter * 32 + lane;  // key row inside the tile = TMEM lane
     const int key = k0 + kr;             // token index inside the sequence
     const bool inner_key = key >= 1 && key <= n;
-    const bool edge_key = key == 0 || key == len - 1;  // supplies the row-sum term
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const float c = p.scale * kLog2e;
+    const uint32_t t_s = tmem + lane_off + qh * kQHalf;
+    const uint64_t c2 = f2_pack(p.scale * kLog2e, p.scale * kLog2e);
     float* const rbase = p.r + p.r_off[b] + static_cast<size_t>(p.head_base) * n;
-    for (int t = 0; t < nh; ++t) {
-      const int sb = t % kSBufs;
-      if (!mbar_wait(&s_full[sb], (t / kSBufs) & 1, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t s[kQHalf];
-      tmem_ld32(tmem + sb * kQry + lane_off + qh * kQHalf, s);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);  // the MMA of head t + 4 may overwrite this buffer
+    // Head t's P column: exponents, M^T += w P, and the column sum into r (APC).
+    auto head = [&](const uint32_t (&sv)[kQHalf], int t) {
       const float w = wts[t];
       const float* lrow = lse_s + t * kQry + qh * kQHalf;
-      float* rh = rbase + static_cast<size_t>(heads[t]) * n;
-      // Packed FP32 pairs (fma/add.f32x2) for the exponent, the column sum and M^T += w P.
-      const uint64_t w2 = f2_pack(w, w), c2 = f2_pack(c, c);
+      const uint64_t w2 = f2_pack(w, w);
       uint64_t cs2 = 0ull;
 #pragma unroll
       for (int g = 0; g < kQHalf / 4; ++g) {
         const float4 l4 = *reinterpret_cast<const float4*>(lrow + 4 * g);
         float a0, a1, a2, a3;
-        f2_unpack(f2_fma(f2_pack(__uint_as_float(s[4 * g]), __uint_as_float(s[4 * g + 1])), c2, f2_pack(l4.x, l4.y)),
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[4 * g]), __uint_as_float(sv[4 * g + 1])), c2, f2_pack(l4.x, l4.y)),
                   a0, a1);
-        f2_unpack(f2_fma(f2_pack(__uint_as_float(s[4 * g + 2]), __uint_as_float(s[4 * g + 3])), c2,
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[4 * g + 2]), __uint_as_float(sv[4 * g + 3])), c2,
                          f2_pack(l4.z, l4.w)),
                   a2, a3);
         // One exponential in four on the FP32 pipe, the rest on the special-function unit.
@@ -248,31 +240,24 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
         acc2[2 * g] = f2_fma(w2, p01, acc2[2 * g]);
         acc2[2 * g + 1] = f2_fma(w2, p23, acc2[2 * g + 1]);
       }
-      float cs[2];
-      {
-        float x0, x1;
-        f2_unpack(cs2, x0, x1);
-        cs[0] = x0;
-        cs[1] = x1;
+      float x0, x1;
+      f2_unpack(cs2, x0, x1);
+      if (inner_key) atomicAdd(rbase + static_cast<size_t>(heads[t]) * n + (key - 1), x0 + x1);
+    };
+    for (int t = 0; t < nh; ++t) {
+      const int sb = t % kSBufs;
+      if (!mbar_wait(&s_full[sb], (t / kSBufs) & 1, p.err, kDevTimeoutEpilogue)) {
+        ok = false;
+        break;
       }
-      // rowsum_i over the inner keys = 1 - P[i, 0] - P[i, L-1] for every inner query i. The lane
-      // that owns key 0 (or L-1) hands its 32 probabilities to the lanes of the warp, one query
-      // each, so the update is one coalesced reduction instead of 32 from a single thread.
-      unsigned edges = __ballot_sync(0xffffffffu, edge_key);
-      while (edges) {
-        const int src = __ffs(edges) - 1;
-        edges &= edges - 1;
-        float mine = 0.0f;
-#pragma unroll
-        for (int u = 0; u < kQHalf; ++u) {
-          const float pu = __shfl_sync(0xffffffffu, fast_exp2(fmaf(__uint_as_float(s[u]), c, lrow[u])), src);
-          if (lane == u) mine = pu;
-        }
-        const int src_key = k0 + (warp & 3) * 32 + src;
-        const int i = q0 + qh * kQHalf + lane;
-        if (i >= 1 && i <= n) atomicAdd(rh + (i - 1), (src_key == 0 ? 1.0f : 0.0f) - mine);
-      }
-      if (inner_key) atomicAdd(rh + (key - 1), cs[0] + cs[1]);
+      tc_fence_after();
+      uint32_t sv[kQHalf];
+      tmem_ld32(t_s + sb * kQry, sv);
+      tmem_ld_wait_regs(sv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);  // the MMA of head t + 4 may overwrite this buffer
+      head(sv, t);
     }
   }
   // Every role is done with the operand ring (loads landed, MMAs complete) past this barrier.
@@ -329,6 +314,50 @@ __global__ void __launch_bounds__(kThreadsCt, 2)
 
 }  // namespace
 
+// The row-sum half of the APC sums for every inner query i and contributing head h:
+// r_h[i] += 1 - P[i, 0] - P[i, L-1], with P[i, k] = exp2(q_i . k_k * scale * log2(e) - lse_i log2(e))
+// from the same fp16 Q and K and the attention's log-sum-exp (rows of P sum to one over all L keys).
+// One thread per token; heads in a loop. Runs after contact_tc_kernel of the layer, on the same
+// stream, so the plain read-modify-write of r does not meet that kernel's atomic column sums.
+__global__ void contact_rowsum_kernel(const ContactParams p, const int32_t* __restrict__ seq_of) {
+  const int tok = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tok >= p.T) return;
+  const int b = seq_of[tok];
+  const int start = p.cu_seqlens[b], len = p.cu_seqlens[b + 1] - start, n = len - 2;
+  const int i = tok - start;
+  if (i < 1 || i > n) return;
+  const float c = p.scale * kLog2e;
+  const size_t ld = static_cast<size_t>(3) * p.d;
+  const __half* q = p.qkv + static_cast<size_t>(tok) * ld;
+  const __half* k0 = p.qkv + static_cast<size_t>(start) * ld + p.d;
+  const __half* k1 = p.qkv + static_cast<size_t>(start + len - 1) * ld + p.d;
+  float* rb = p.r + p.r_off[b] + static_cast<size_t>(p.head_base) * n + (i - 1);
+  for (int h = 0; h < p.H; ++h) {
+    const float w = p.w_layer[h];
+    if (w == 0.0f) continue;
+    float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+    for (int e = 0; e < kD; e += 8) {
+      const uint4 qv = *reinterpret_cast<const uint4*>(q + h * kD + e);
+      const uint4 av = *reinterpret_cast<const uint4*>(k0 + h * kD + e);
+      const uint4 bv = *reinterpret_cast<const uint4*>(k1 + h * kD + e);
+      const __half2* qh = reinterpret_cast<const __half2*>(&qv);
+      const __half2* ah = reinterpret_cast<const __half2*>(&av);
+      const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 qf = __half22float2(qh[u]), af = __half22float2(ah[u]), bf = __half22float2(bh[u]);
+        d0 = fmaf(qf.x, af.x, fmaf(qf.y, af.y, d0));
+        d1 = fmaf(qf.x, bf.x, fmaf(qf.y, bf.y, d1));
+      }
+    }
+    const float l2 = p.lse[static_cast<size_t>(h) * p.T + tok] * kLog2e;
+    const float p0 = fast_exp2(fmaf(d0, c, -l2));
+    const float p1 = fast_exp2(fmaf(d1, c, -l2));
+    rb[static_cast<size_t>(h) * n] += (1.0f - p0) - p1;
+  }
+}
+
 int contact_tc_tiles(int len, int4* out, int b) {
   const int kt = (len + kKeys - 1) / kKeys, qt = (len + kQry - 1) / kQry;
   if (out)
@@ -338,7 +367,7 @@ int contact_tc_tiles(int len, int4* out, int b) {
 }
 
 cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q64, const ContactParams& p,
-                              cudaStream_t s) {
+                              const int32_t* seq_of, cudaStream_t s) {
   if (p.n_tiles <= 0) return cudaSuccess;
   if (p.dh != kD || p.H > kMaxHeads) return cudaErrorInvalidValue;
   const int smem = contact_tc_smem_bytes(p.H);
@@ -353,6 +382,9 @@ cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_
     if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   contact_tc_kernel<<<p.n_tiles, kThreadsCt, smem, s>>>(tm_k128, tm_q64, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  contact_rowsum_kernel<<<(p.T + 127) / 128, 128, 0, s>>>(p, seq_of);
   return cudaGetLastError();
 }
 

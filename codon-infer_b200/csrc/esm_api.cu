@@ -29,15 +29,15 @@ struct esm_ctx {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   int cta_pair = 1;  // GEMM tiles on CTA pairs (cta_group::2); ESM_GEMM_CTA_PAIR=0 selects single CTAs
-  // Attention kernel for head_dim 64 (ESM_ATTN_TC): 3 = tcgen05, two query tiles per CTA, 32-key
-  // tiles with two score buffers per tile (measured fastest); 2 = the same with 64-key tiles and one
-  // score buffer; 1 = tcgen05, one query tile per CTA; 0 = the mma.sync kernel.
+  // Attention kernel for head_dim 64 and 32 (ESM_ATTN_TC): 3 = tcgen05, two 128-row query tiles
+  // per CTA sharing 32-key K/V tiles, two score buffers per tile (the default); 0 = the mma.sync
+  // kernel (also the one for head_dim 16 and 24).
   int attn_tc = 3;
-  // Eighths of the softmax exponentials on the FP32 pipe (ESM_ATTN_POLY, 0..4); -1 = the kernel's
-  // measured best (2 for kernel 3 with packed arithmetic, 0 otherwise).
+  // Eighths of the softmax exponentials on the FP32 pipe (ESM_ATTN_POLY, 0..3); -1 = the kernel's
+  // measured best (2 with packed arithmetic, 0 otherwise).
   int attn_poly = -1;
-  // Softmax arithmetic of kernel 3 (ESM_ATTN_EXP): 0 scalar FP32, 1 packed FP32 pairs (default,
-  // measured fastest), 2 fp16-pair exponentials.
+  // Softmax arithmetic (ESM_ATTN_EXP): 0 scalar FP32, 1 packed FP32 pairs (default, measured
+  // fastest), 2 fp16-pair exponentials.
   int attn_exp = 1;
   int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
@@ -88,7 +88,6 @@ struct esm_ctx {
   int32_t* cu = nullptr;
   float* escale = nullptr;
   int2* work = nullptr;
-  int2* work128 = nullptr;
   int2* work256 = nullptr;
   int4* ctiles = nullptr;
   int64_t* m_off = nullptr;
@@ -105,14 +104,13 @@ struct esm_ctx {
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
-  int2* h_work128 = nullptr;
   int2* h_work256 = nullptr;
   int4* h_tiles = nullptr;
   int64_t* h_moff = nullptr;
   int64_t* h_roff = nullptr;
   cudaEvent_t plan_ev = nullptr;
   std::vector<int32_t> plan_key;
-  int plan_work = 0, plan_work128 = 0, plan_work256 = 0, plan_tiles = 0;
+  int plan_work = 0, plan_work256 = 0, plan_tiles = 0;
   // instrumentation: CUDA event pairs around each launch while profiling is on
   struct ProfRec {
     cudaEvent_t a, b;
@@ -170,13 +168,12 @@ void free_list(std::vector<void*>& list) {
 }
 
 void free_pinned(esm_ctx* c) {
-  for (void* p : {static_cast<void*>(c->h_cu), static_cast<void*>(c->h_work), static_cast<void*>(c->h_work128),
+  for (void* p : {static_cast<void*>(c->h_cu), static_cast<void*>(c->h_work),
                   static_cast<void*>(c->h_work256),
                   static_cast<void*>(c->h_tiles), static_cast<void*>(c->h_moff), static_cast<void*>(c->h_roff)})
     if (p) cudaFreeHost(p);
   c->h_cu = nullptr;
   c->h_work = nullptr;
-  c->h_work128 = nullptr;
   c->h_work256 = nullptr;
   c->h_tiles = nullptr;
   c->h_moff = nullptr;
@@ -409,7 +406,6 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   A(&c->cu, max_seqs + 1);
   A(&c->escale, max_seqs);
   A(&c->work, c->work_cap);
-  A(&c->work128, c->work_cap);
   A(&c->work256, c->work_cap);
   A(&c->ctiles, c->tiles_cap);
   A(&c->m_off, max_seqs);
@@ -436,7 +432,6 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   }
   ESM_CUDA(cudaMallocHost(&c->h_cu, sizeof(int32_t) * (max_seqs + 1)));
   ESM_CUDA(cudaMallocHost(&c->h_work, sizeof(int2) * c->work_cap));
-  ESM_CUDA(cudaMallocHost(&c->h_work128, sizeof(int2) * c->work_cap));
   ESM_CUDA(cudaMallocHost(&c->h_work256, sizeof(int2) * c->work_cap));
   ESM_CUDA(cudaMallocHost(&c->h_tiles, sizeof(int4) * c->tiles_cap));
   ESM_CUDA(cudaMallocHost(&c->h_moff, sizeof(int64_t) * max_seqs));
@@ -476,7 +471,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   const int64_t hl = static_cast<int64_t>(g.n_layers) * g.n_heads;
   // The previous plan's copies must have left the pinned staging before it is rewritten.
   if (c->plan_ev) ESM_CUDA(cudaEventSynchronize(c->plan_ev));
-  int nw = 0, nw128 = 0, nw256 = 0, nt = 0;
+  int nw = 0, nw256 = 0, nt = 0;
   int64_t moff = 0, roff = 0;
   for (int b = 0; b <= B; ++b) c->h_cu[b] = h_cu[b];
   for (int b = 0; b < B; ++b) {
@@ -484,7 +479,6 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
     const int qt = (len + 63) / 64;
     if (nw + qt > c->work_cap) return fail(c, ESM_ECAPACITY, "attention work list exceeds the reserved capacity");
     for (int t = 0; t < qt; ++t) c->h_work[nw++] = make_int2(b, t);
-    for (int t = 0; t < (len + 127) / 128; ++t) c->h_work128[nw128++] = make_int2(b, t);
     for (int t = 0; t < (len + 255) / 256; ++t) c->h_work256[nw256++] = make_int2(b, t);
     if (contacts) {
       const int64_t n = std::max(len - 2, 0);
@@ -509,7 +503,6 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
     return fail(c, ESM_ECAPACITY, "contact maps exceed the reserved capacity");
   ESM_CUDA(cudaMemcpyAsync(c->cu, c->h_cu, sizeof(int32_t) * (B + 1), cudaMemcpyHostToDevice, s));
   ESM_CUDA(cudaMemcpyAsync(c->work, c->h_work, sizeof(int2) * nw, cudaMemcpyHostToDevice, s));
-  ESM_CUDA(cudaMemcpyAsync(c->work128, c->h_work128, sizeof(int2) * nw128, cudaMemcpyHostToDevice, s));
   ESM_CUDA(cudaMemcpyAsync(c->work256, c->h_work256, sizeof(int2) * nw256, cudaMemcpyHostToDevice, s));
   if (contacts) {
     ESM_CUDA(cudaMemcpyAsync(c->m_off, c->h_moff, sizeof(int64_t) * B, cudaMemcpyHostToDevice, s));
@@ -520,7 +513,6 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
   ESM_CUDA(cudaEventRecord(c->plan_ev, s));
   c->plan_key = key;
   c->plan_work = nw;
-  c->plan_work128 = nw128;
   c->plan_work256 = nw256;
   c->plan_tiles = nt;
   return ESM_OK;
@@ -641,18 +633,12 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
-  // head_dim 64 runs every tcgen05 kernel; head_dim 32 the two-tile ones (3: double-buffered,
-  // the default; any other ESM_ATTN_TC > 0: 64-key tiles).
-  const int attn_tc = dh == 64 ? c->attn_tc : (dh == 32 && c->attn_tc > 0 ? (c->attn_tc == 3 ? 3 : 2) : 0);
-  const CUtensorMap& tm_att_q = dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q;
-  const CUtensorMap& tm_att_kv = dh == 32 ? c->tm_qkv_kv32 : c->tm_qkv_kv;
-  esm::AttnParams ap128 = ap;
-  ap128.work = c->work128;
-  ap128.n_work = c->plan_work128;
+  // head_dim 64 and 32 run the tcgen05 kernel (attention_tc3.cu) unless ESM_ATTN_TC=0; head_dim
+  // 16 and 24 the mma.sync kernel (attention.cu).
+  const bool attn_tc = (dh == 64 || dh == 32) && c->attn_tc != 0;
   esm::AttnParams ap256 = ap;
   ap256.work = c->work256;
   ap256.n_work = c->plan_work256;
-
 
   for (int l = 0; l < nl; ++l) {
     esm::LayerSrc src{};
@@ -681,15 +667,11 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
-      if (attn_tc == 3) {
+      if (attn_tc) {
         const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 ? 2 : 0);
         ESM_CUDA(esm::launch_attention_tc3(dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q,
                                            dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32, ap256, poly, c->attn_exp,
                                            s));
-      } else if (attn_tc == 2) {
-        ESM_CUDA(esm::launch_attention_tc2(tm_att_q, tm_att_kv, ap256, std::max(0, c->attn_poly), s));
-      } else if (attn_tc) {
-        ESM_CUDA(esm::launch_attention_tc(c->tm_qkv_q, c->tm_qkv_kv, ap128, s));
       } else {
         ESM_CUDA(esm::launch_attention(ap, s));
       }
@@ -715,7 +697,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       cp.head_base = l * H;
       cp.err = c->d_err;
       if (use_contact_tc(c)) {
-        ESM_CUDA(esm::launch_contact_tc(c->tm_qkv_q, c->tm_qkv_kv, cp, s));
+        ESM_CUDA(esm::launch_contact_tc(c->tm_qkv_q, c->tm_qkv_kv, cp, c->seq_of, s));
       } else {
         ESM_CUDA(esm::launch_contact_accumulate(cp, s));
       }
@@ -897,7 +879,7 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   c->num_sms = prop.multiProcessorCount;
   if (const char* v = std::getenv("ESM_GEMM_CTA_PAIR")) c->cta_pair = std::atoi(v) != 0;
   if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v);
-  if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(4, std::max(0, std::atoi(v)));
+  if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(3, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(2, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||

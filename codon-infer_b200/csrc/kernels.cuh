@@ -85,17 +85,9 @@ struct AttnParams {
   float scale;             // 1/sqrt(dh)
   int* err;                // device error word (bounded waits of the tcgen05 kernel)
 };
+// mma.sync attention (attention.cu): work items are (sequence, 64-row query tile); any head_dim
+// that is a multiple of 8 up to 64.
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s);
-// tcgen05 attention for head_dim 64: work items are (sequence, 128-row query tile); tm_q / tm_kv
-// are fp16 tensor maps over qkv [T, 3d] with 64-column boxes of 128 / 64 rows.
-cudaError_t launch_attention_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
-                                cudaStream_t s);
-// Same with two 128-row query tiles per CTA (attention_tc2.cu): work items are (sequence, 256-row
-// query block); poly_eighths (0..4) of the softmax exponentials are computed on the FP32 pipe.
-cudaError_t launch_attention_tc2(const CUtensorMap& tm_q, const CUtensorMap& tm_kv, const AttnParams& p,
-                                 int poly_eighths, cudaStream_t s);
-// Same with 32-key K/V tiles and two score buffers per query tile (attention_tc3.cu, head_dim 64 or
-// 32): tm_kv32 boxes are 32 rows x head_dim columns (128- or 64-byte swizzle, as tm_q).
 // BlockQ8_0 / BlockQ4_0 quantization of nblocks x 32 FP32 values on the device (quantize.cu);
 // dtype 1 = Q8_0, 2 = Q4_0; src 16-byte aligned, dst 4-byte aligned.
 cudaError_t launch_quantize(int dtype, const float* src, int64_t nblocks, uint8_t* dst, cudaStream_t s);
@@ -104,8 +96,14 @@ cudaError_t launch_quantize(int dtype, const float* src, int64_t nblocks, uint8_
 int64_t contact_rank_scratch_keys(int n, int k);
 cudaError_t launch_contact_rank(const float* map, int n, int min_sep, int k, uint64_t* scratch, uint64_t* out_keys,
                                 cudaStream_t s);
+// tcgen05 attention for head_dim 64 or 32 (attention_tc3.cu): work items are (sequence, 256-row
+// query block); two 128-row query tiles share every 32-key K/V tile and have two score buffers
+// each. tm_q: qkv map with head_dim-column boxes of 128 rows; tm_kv32: the same with 32 rows
+// (128- or 64-byte swizzle). poly_eighths (0..3) of the exponential pairs run on the FP32 pipe;
+// exp_mode: 0 scalar FP32, 1 packed FP32 pairs, 2 fp16-pair exponentials.
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s);
+
 
 // Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
 // recomputes P = softmax(q k^T * scale) tile by tile from the saved LSE, adds w * P into the
@@ -134,8 +132,9 @@ cudaError_t launch_contact_accumulate(const ContactParams& p, cudaStream_t s);
 // not null) and returns its length. tm_k128 / tm_q64: qkv [T, 3d] maps with 64-column boxes of 128
 // and 64 rows.
 int contact_tc_tiles(int len, int4* out, int b);
+// Also launches the row-sum pass (contact_rowsum_kernel; seq_of [T] maps a token to its sequence).
 cudaError_t launch_contact_tc(const CUtensorMap& tm_k128, const CUtensorMap& tm_q64, const ContactParams& p,
-                              cudaStream_t s);
+                              const int32_t* seq_of, cudaStream_t s);
 
 // contacts = sigmoid(M + M^T - sum_h a_h r_h r_h^T + b) with a_h = w_h / T_h (APC), per sequence.
 cudaError_t launch_contact_finalize(const float* M, const float* r, const int64_t* m_off, const int64_t* r_off,

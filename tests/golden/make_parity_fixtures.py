@@ -15,7 +15,7 @@ these committed outputs instead of running it:
                  entries, the two corner blocks whole, and every row's sum.
   parity_c3.npz  ESM-2 150M FP32 masked-marginal scan of the 300-residue wild type: 16 positions
                  spread over the sequence, their [20] deltas and entropy (run_pipeline_dms_with_mode,
-                 src/pipeline.rs:109-175), and the full logits of two variants.
+                 src/pipeline.rs:109-175), and the full logits of those 16 variants.
 
 Nothing here needs the reference checkout or a GPU.
 """
@@ -93,11 +93,9 @@ def make_c3() -> None:
         toks = synth.dms_variant(wt, p)
         lg = oracle.forward(cfg, c["dtype"], t, toks)["logits"]
         deltas[k], ent[k] = oracle.dms_scores(lg[p + 1], int(wt[p]))
-        if p in (0, 150):
-            full.append(lg)
+        full.append(lg)
     np.savez_compressed(HERE / "parity_c3.npz", wildtype=wt, positions=np.array(C3_POSITIONS, np.int32),
-                        deltas=deltas, entropy=ent, variant_logits=np.stack(full),
-                        variant_positions=np.array([0, 150], np.int32))
+                        deltas=deltas, entropy=ent, variant_logits=np.stack(full))
 
 
 if __name__ == "__main__":

@@ -354,16 +354,14 @@ def test_contact_kernels_agree(esm, monkeypatch):
     assert np.abs(maps[0] - maps[1]).max() <= 2e-4
 
 
-@pytest.mark.parametrize("attn,poly,exp", [("1", "0", "0"), ("2", "0", "0"), ("2", "2", "0"), ("2", "4", "0"),
-                                           ("3", "0", "0"), ("3", "2", "0"), ("3", "0", "1"), ("3", "2", "1"),
-                                           ("3", "0", "2")])
+@pytest.mark.parametrize("attn,poly,exp", [("3", "0", "0"), ("3", "2", "0"), ("3", "3", "0"), ("3", "0", "1"),
+                                           ("3", "2", "1"), ("3", "0", "2"), ("0", "0", "0")])
 def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly, exp):
-    # The tcgen05 attention kernels (ESM_ATTN_TC=1: one 128-row query tile per CTA; 2: two tiles
-    # per CTA sharing K/V, P in tensor memory; 3: the same with 32-key tiles and two score buffers
-    # per tile; ESM_ATTN_POLY eighths of the exponentials on the FP32 pipe; ESM_ATTN_EXP the softmax
-    # arithmetic of kernel 3: scalar, packed FP32 pairs, fp16-pair exponentials) on lengths at and
-    # around the 32/64-key and 128/256-row tile edges, with contacts (which read the saved
-    # log-sum-exp).
+    # The tcgen05 attention kernel (ESM_ATTN_TC=3, the default: two 128-row query tiles sharing
+    # 32-key K/V tiles, two score buffers per tile; ESM_ATTN_POLY eighths of the exponentials on the
+    # FP32 pipe; ESM_ATTN_EXP the softmax arithmetic: scalar, packed FP32 pairs, fp16-pair
+    # exponentials) and the mma.sync kernel (ESM_ATTN_TC=0) on lengths at and around the 32-key and
+    # 128/256-row tile edges, with contacts (which read the saved log-sum-exp).
     monkeypatch.setenv("ESM_ATTN_TC", attn)
     monkeypatch.setenv("ESM_ATTN_POLY", poly)
     monkeypatch.setenv("ESM_ATTN_EXP", exp)
@@ -399,11 +397,11 @@ def test_preallocated_outputs(esm):
     m.close()
 
 
-@pytest.mark.parametrize("attn", ["3", "2"])
+@pytest.mark.parametrize("attn", ["3", "0"])
 def test_150m_shape_head_dim_32_attention(esm, orc, monkeypatch, attn):
-    # head_dim 32 (ESM-2 150M) on the two-tile tcgen05 attention kernels (64-byte-swizzled tiles;
-    # 3: 32-key tiles with two score buffers per tile, the default; 2: 64-key tiles), with contacts
-    # reading the log-sum-exp, on lengths around the 32/64-key and 128/256-row tile edges.
+    # head_dim 32 (ESM-2 150M) on the tcgen05 attention kernel (3: 64-byte-swizzled tiles, the
+    # default) and on the mma.sync kernel (0), with contacts reading the log-sum-exp, on lengths
+    # around the 32/64-key and 128/256-row tile edges.
     monkeypatch.setenv("ESM_ATTN_TC", attn)
     base = esm.esm2_150m()
     cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
@@ -413,3 +411,29 @@ def test_150m_shape_head_dim_32_attention(esm, orc, monkeypatch, attn):
     seqs = esm.random_sequences(len(lens), lens, seed=13)
     out = m.forward(seqs, want_hidden=True, want_contacts=True)
     compare(orc, cfg, esm.DTYPE_FP32, t, seqs, out, cw)
+
+
+@pytest.mark.parametrize("attn", ["3", "0"])
+def test_attention_rescale_path(esm, orc, monkeypatch, attn):
+    # Query and key weights three times larger than the other tests' give scaled scores whose row
+    # maxima grow by more than 2^8 (in the exp2 domain) from one 128-key block to the next in about
+    # a tenth of the rows of the 640-token sequence (counted offline from the same weights), so the
+    # lazy rescale of O runs there (the 32-key tiles of the tcgen05 kernel see at least as many).
+    monkeypatch.setenv("ESM_ATTN_TC", attn)
+    base = esm.esm2_650m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    t32 = esm.synth_fp32_tensors(cfg, seed=14, bias_std=0.02, ln_jitter=0.1)
+    t32["wq"] = (t32["wq"] * 3).astype(np.float32)
+    t32["wk"] = (t32["wk"] * 3).astype(np.float32)
+    t = esm.quantize_tensors(t32, esm.DTYPE_Q4_0)
+    m = esm.Model(0)
+    m.load_tensors(cfg, esm.DTYPE_Q4_0, t)
+    rng = np.random.default_rng(15)
+    cw = (rng.standard_normal(cfg.n_layers * cfg.n_heads) * 0.1).astype(np.float32)
+    m.set_contact_head(cw, -0.5)
+    lens = [300, 640, 129]
+    m.reserve(sum(lens), len(lens), 640, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=16)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
+
