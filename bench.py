@@ -42,6 +42,12 @@ import synth  # noqa: E402  (numpy only: no native library is loaded by this imp
 
 UNIT = "residues/s"
 CONFIGS = synth.CONFIGS
+_json_out = sys.stdout
+
+
+def emit(line: dict) -> None:
+    _json_out.write(json.dumps(line) + "\n")
+    _json_out.flush()
 
 
 def metric_name(cfg_name, c):
@@ -194,7 +200,7 @@ def run_reference(args):
                          "sample": cpu_sample_desc(c, cfg)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def timed_loop(step, steps, stream, dev, world, dist):
@@ -470,13 +476,19 @@ def run_ours(args):
             line["strong_scaling"] = strong
         if c["dms"]:
             line["dms_variants_per_s"] = batch * e2e_steps / e2e_s
-        print(json.dumps(line), flush=True)
+        emit(line)
     model.close()
     if world > 1:
         dist.destroy_process_group()
 
 
 def main():
+    # The JSON line is the only thing on stdout: everything else written to file descriptor 1
+    # (library banners such as NCCL's version line at communicator set-up) goes to stderr.
+    global _json_out
+    _json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
