@@ -55,11 +55,18 @@ struct esm_ctx {
   float* bqkv = nullptr;         // [nl, 3d]
   float* emb_f32 = nullptr;      // [V, d] fp32 embedding (dequantized copy for Q8 models)
   __half* dense16 = nullptr;     // LM-head dense weight in fp16 [d, d]
-  __half* wqkv16 = nullptr;      // per-layer fp16 scratch
-  __half* wo16 = nullptr;
-  __half* w116 = nullptr;
-  __half* w216 = nullptr;
-  CUtensorMap tm_wqkv, tm_wo, tm_w1, tm_w2, tm_dense;
+  // Per-layer fp16 weight scratch, two sets: layer l + 1 is dequantised into set (l + 1) & 1 on
+  // the side stream while layer l computes with set l & 1.
+  __half* wqkv16[2] = {};
+  __half* wo16[2] = {};
+  __half* w116[2] = {};
+  __half* w216[2] = {};
+  CUtensorMap tm_wqkv[2], tm_wo[2], tm_w1[2], tm_w2[2], tm_dense;
+  // The side stream of the dequantisation and its events: ev_deq[b] = set b written, ev_read[b] =
+  // the layer that read set b is done. ESM_DEQUANT_OVERLAP=0 dequantises in the forward's stream.
+  int deq_overlap = 1;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_deq[2] = {}, ev_read[2] = {};
   int bn_qkv = 0, bn_o = 0, bn_fc1 = 0, bn_fc2 = 0, bn_dense = 0;
 
   // ---- contact head ----
@@ -218,10 +225,12 @@ int build_weight_maps(esm_ctx* c) {
   c->bn_fc2 = esm::gemm_pick_bn(d, 0);
   c->bn_dense = esm::gemm_pick_bn(d, 0);
   // Weight (B operand) maps load half tiles: bn/2 rows per box.
-  bool ok = esm::make_tmap_f16(&c->tm_wqkv, c->wqkv16, 3 * d, d, d, c->bn_qkv / 2) &&
-            esm::make_tmap_f16(&c->tm_wo, c->wo16, d, d, d, c->bn_o / 2) &&
-            esm::make_tmap_f16(&c->tm_w1, c->w116, F, d, d, c->bn_fc1 / 2) &&
-            esm::make_tmap_f16(&c->tm_w2, c->w216, d, F, F, c->bn_fc2 / 2);
+  bool ok = true;
+  for (int b = 0; b < 2; ++b)
+    ok = ok && esm::make_tmap_f16(&c->tm_wqkv[b], c->wqkv16[b], 3 * d, d, d, c->bn_qkv / 2) &&
+         esm::make_tmap_f16(&c->tm_wo[b], c->wo16[b], d, d, d, c->bn_o / 2) &&
+         esm::make_tmap_f16(&c->tm_w1[b], c->w116[b], F, d, d, c->bn_fc1 / 2) &&
+         esm::make_tmap_f16(&c->tm_w2[b], c->w216[b], d, F, F, c->bn_fc2 / 2);
   if (ok && c->has_head) ok = esm::make_tmap_f16(&c->tm_dense, c->dense16, d, d, d, c->bn_dense / 2);
   return ok ? ESM_OK : fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for a weight matrix");
 }
@@ -336,10 +345,13 @@ int load_host_impl(esm_ctx* c, const esm_config& cfg, int dtype, const void* con
     const float* dense_w = static_cast<const float*>(c->w[19]) + 2 * d;
     ESM_CUDA(esm::launch_to_f16(ESM_DTYPE_FP32, dense_w, d * d, c->dense16, c->stream));
   }
-  int rc = dev_alloc(c, c->w_allocs, &c->wqkv16, static_cast<size_t>(3 * d * d));
-  if (!rc) rc = dev_alloc(c, c->w_allocs, &c->wo16, static_cast<size_t>(d * d));
-  if (!rc) rc = dev_alloc(c, c->w_allocs, &c->w116, static_cast<size_t>(F * d));
-  if (!rc) rc = dev_alloc(c, c->w_allocs, &c->w216, static_cast<size_t>(d * F));
+  int rc = ESM_OK;
+  for (int b = 0; b < 2 && !rc; ++b) {
+    rc = dev_alloc(c, c->w_allocs, &c->wqkv16[b], static_cast<size_t>(3 * d * d));
+    if (!rc) rc = dev_alloc(c, c->w_allocs, &c->wo16[b], static_cast<size_t>(d * d));
+    if (!rc) rc = dev_alloc(c, c->w_allocs, &c->w116[b], static_cast<size_t>(F * d));
+    if (!rc) rc = dev_alloc(c, c->w_allocs, &c->w216[b], static_cast<size_t>(d * F));
+  }
   if (rc) return rc;
   rc = build_weight_maps(c);
   if (rc) return rc;
@@ -640,7 +652,13 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap256.work = c->work256;
   ap256.n_work = c->plan_work256;
 
-  for (int l = 0; l < nl; ++l) {
+  // Weight dequantisation of layer l into fp16 set l & 1: on the side stream, one layer ahead of
+  // the layer that uses it, after the layer that last read that set; the forward's stream waits
+  // for it before the layer's first GEMM. The side stream starts after the work already queued on
+  // the forward's stream and every side-stream launch is joined back into that stream.
+  const bool overlap = c->deq_overlap != 0;
+  cudaStream_t ds = overlap ? c->side : s;
+  auto dequant = [&](int l) -> int {
     esm::LayerSrc src{};
     for (int m = 0; m < 6; ++m) src.dtype[m] = m < 4 ? dt_mat : dt_fc;
     src.w[0] = static_cast<const uint8_t*>(c->w[3]) + l * mat_b;
@@ -651,9 +669,32 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     src.w[5] = static_cast<const uint8_t*>(c->w[15]) + l * fc_b;
     src.elems[0] = src.elems[1] = src.elems[2] = src.elems[3] = dd;
     src.elems[4] = src.elems[5] = fd;
+    const int b = l & 1;
+    if (overlap) ESM_CUDA(cudaStreamWaitEvent(ds, c->ev_read[b], 0));
     {
-      ProfScope ps(c, s, ESM_PROF_DEQUANT, 0.0, static_cast<double>(4 * mat_b + 2 * fc_b) + 2.0 * (4 * dd + 2 * fd));
-      ESM_CUDA(esm::launch_dequant_layer(src, c->wqkv16, c->wo16, c->w116, c->w216, s));
+      ProfScope ps(c, ds, ESM_PROF_DEQUANT, 0.0, static_cast<double>(4 * mat_b + 2 * fc_b) + 2.0 * (4 * dd + 2 * fd));
+      ESM_CUDA(esm::launch_dequant_layer(src, c->wqkv16[b], c->wo16[b], c->w116[b], c->w216[b], ds));
+    }
+    if (overlap) ESM_CUDA(cudaEventRecord(c->ev_deq[b], ds));
+    return ESM_OK;
+  };
+  if (overlap) {
+    ESM_CUDA(cudaEventRecord(c->ev_start, s));
+    ESM_CUDA(cudaStreamWaitEvent(ds, c->ev_start, 0));
+    rc = dequant(0);
+    if (rc) return rc;
+  }
+  for (int l = 0; l < nl; ++l) {
+    const int wb = l & 1;
+    if (overlap) {
+      if (l + 1 < nl) {
+        rc = dequant(l + 1);
+        if (rc) return rc;
+      }
+      ESM_CUDA(cudaStreamWaitEvent(s, c->ev_deq[wb], 0));
+    } else {
+      rc = dequant(l);
+      if (rc) return rc;
     }
     if (l > 0) {
       ProfScope ps(c, s, ESM_PROF_NORM, 0.0, rowb * 6.0);
@@ -661,7 +702,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * 3.0 * d * d, 0.0);
-      rc = gemm(c, c->tm_xn, c->tm_wqkv, out_qkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d,
+      rc = gemm(c, c->tm_xn, c->tm_wqkv[wb], out_qkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d,
                 c->bqkv + static_cast<int64_t>(l) * 3 * d, c->qkv, 3 * d, s);
       if (rc) return rc;
     }
@@ -704,7 +745,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(dd), 0.0);
-      rc = gemm(c, c->tm_ao, c->tm_wo, out_x, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d,
+      rc = gemm(c, c->tm_ao, c->tm_wo[wb], out_x, c->bn_o, esm::kEpiResidF32, T, d, d, bo + static_cast<int64_t>(l) * d, c->x, d,
                 s);
       if (rc) return rc;
     }
@@ -714,16 +755,17 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(fd), 0.0);
-      rc = gemm(c, c->tm_xn, c->tm_w1, out_hb, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb,
+      rc = gemm(c, c->tm_xn, c->tm_w1[wb], out_hb, c->bn_fc1, esm::kEpiGeluF16, T, F, d, fc1_b + static_cast<int64_t>(l) * F, c->hb,
                 F, s);
       if (rc) return rc;
     }
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * static_cast<double>(fd), 0.0);
-      rc = gemm(c, c->tm_hb, c->tm_w2, out_x, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x,
+      rc = gemm(c, c->tm_hb, c->tm_w2[wb], out_x, c->bn_fc2, esm::kEpiResidF32, T, d, F, fc2_b + static_cast<int64_t>(l) * d, c->x,
                 d, s);
       if (rc) return rc;
     }
+    if (overlap) ESM_CUDA(cudaEventRecord(c->ev_read[wb], s));
     if (d_layer_hidden)
       ESM_CUDA(cudaMemcpyAsync(d_layer_hidden + static_cast<int64_t>(l) * T * d, c->x, static_cast<size_t>(T) * d * 4,
                                cudaMemcpyDeviceToDevice, s));
@@ -882,10 +924,22 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(3, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(2, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
-  if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+  if (const char* v = std::getenv("ESM_DEQUANT_OVERLAP")) c->deq_overlap = std::atoi(v) != 0;
+  bool events_ok = cudaSetDevice(device) == cudaSuccess &&
+                   cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) == cudaSuccess;
+  for (int b = 0; b < 2 && events_ok; ++b)
+    events_ok = cudaEventCreateWithFlags(&c->ev_deq[b], cudaEventDisableTiming) == cudaSuccess &&
+                cudaEventCreateWithFlags(&c->ev_read[b], cudaEventDisableTiming) == cudaSuccess;
+  if (!events_ok || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
       cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream) != cudaSuccess ||
       cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    if (c->d_err) cudaFree(c->d_err);
+    for (cudaStream_t st : {c->stream, c->side})
+      if (st) cudaStreamDestroy(st);
+    for (cudaEvent_t e : {c->ev_start, c->ev_deq[0], c->ev_deq[1], c->ev_read[0], c->ev_read[1]})
+      if (e) cudaEventDestroy(e);
     delete c;
     return ESM_ECUDA;
   }
@@ -911,6 +965,12 @@ int esm_ctx_destroy(esm_ctx* c) {
     if (c->plan_ev) cudaEventDestroy(c->plan_ev);
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->d_err) cudaFree(c->d_err);
+    if (c->side) {
+      cudaStreamSynchronize(c->side);
+      cudaStreamDestroy(c->side);
+    }
+    for (cudaEvent_t e : {c->ev_start, c->ev_deq[0], c->ev_deq[1], c->ev_read[0], c->ev_read[1]})
+      if (e) cudaEventDestroy(e);
     cudaStreamDestroy(c->stream);
   }
   delete c;

@@ -437,3 +437,25 @@ def test_attention_rescale_path(esm, orc, monkeypatch, attn):
     out = m.forward(seqs, want_hidden=True, want_contacts=True)
     compare(orc, cfg, esm.DTYPE_Q4_0, t, seqs, out, cw)
 
+
+
+def test_dequantisation_overlap_is_exact(esm, monkeypatch):
+    # Layer l + 1's weights are dequantised on a side stream while layer l computes, into the other
+    # of two fp16 weight sets; with ESM_DEQUANT_OVERLAP=0 the same kernels run in the forward's
+    # stream into one set. Back-to-back forwards of different batches (which reuse both sets) must
+    # give the same logits bit for bit either way.
+    base = esm.esm2_650m()
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 5, base.n_heads, arch=base.arch)
+    t = esm.quantize_tensors(esm.synth_fp32_tensors(cfg, seed=17, bias_std=0.02, ln_jitter=0.1), esm.DTYPE_Q4_0)
+    batches = [esm.random_sequences(3, [200, 64, 130], seed=18), esm.random_sequences(2, [300, 33], seed=19)]
+    outs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ESM_DEQUANT_OVERLAP", flag)
+        m = esm.Model(0)
+        m.load_tensors(cfg, esm.DTYPE_Q4_0, t)
+        m.reserve(400, 3, 300)
+        outs[flag] = [m.forward(b)["logits"].copy() for b in batches + batches]
+        m.check_device()
+        m.close()
+    for a, b in zip(outs["1"], outs["0"]):
+        np.testing.assert_array_equal(a, b)
