@@ -261,11 +261,13 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
   zero_pad_cols<DH>(&sK[0][0], 2, tid, 128);
   __syncthreads();
 
-  // Heads that contribute (non-zero regression weight), as a bitmask of up to 64 heads.
+  // Heads that contribute (non-zero regression weight), up to 64; with several CTAs per tile
+  // (gridDim.y = head groups, when a layer has too few tiles to fill the GPU) this CTA takes every
+  // gridDim.y-th of them.
   int heads[64];
-  int nh = 0;
+  int nh = 0, seen = 0;
   for (int h = 0; h < p.H && h < 64; ++h)
-    if (p.w_layer[h] != 0.0f) heads[nh++] = h;
+    if (p.w_layer[h] != 0.0f && seen++ % gridDim.y == blockIdx.y) heads[nh++] = h;
 
   float acc[8][4];
 #pragma unroll
@@ -346,8 +348,10 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
       }
       __syncthreads();
     }
-    // M[i-1, j-1] += acc over the inner block (each tile is owned by exactly one CTA).
+    // M[i-1, j-1] += acc over the inner block: a plain update when one CTA owns the tile, an
+    // atomic one when the tile's heads are split over several CTAs.
     float* M = p.M + p.m_off[b];
+    const bool shared_tile = gridDim.y > 1;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       const int col = j0 + nt * 8 + (lane & 3) * 2;
@@ -356,8 +360,13 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
         const int row = row_a + 8 * r;
         if (row < 1 || row > n) continue;
         float* mrow = M + static_cast<size_t>(row - 1) * n;
-        if (col >= 1 && col <= n) mrow[col - 1] += acc[nt][2 * r];
-        if (col + 1 >= 1 && col + 1 <= n) mrow[col] += acc[nt][2 * r + 1];
+        if (shared_tile) {
+          if (col >= 1 && col <= n) atomicAdd(mrow + col - 1, acc[nt][2 * r]);
+          if (col + 1 >= 1 && col + 1 <= n) atomicAdd(mrow + col, acc[nt][2 * r + 1]);
+        } else {
+          if (col >= 1 && col <= n) mrow[col - 1] += acc[nt][2 * r];
+          if (col + 1 >= 1 && col + 1 <= n) mrow[col] += acc[nt][2 * r + 1];
+        }
       }
     }
   }
@@ -456,7 +465,8 @@ cudaError_t launch_attention_dh(const AttnParams& p, cudaStream_t s) {
 
 template <int DH>
 cudaError_t launch_contact_dh(const ContactParams& p, cudaStream_t s) {
-  contact_accumulate_kernel<DH><<<p.n_tiles, 128, 0, s>>>(p);
+  const int groups = p.head_groups > 1 ? p.head_groups : 1;
+  contact_accumulate_kernel<DH><<<dim3(p.n_tiles, groups), 128, 0, s>>>(p);
   return cudaGetLastError();
 }
 

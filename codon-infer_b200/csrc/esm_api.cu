@@ -737,6 +737,10 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       cp.r = c->r;
       cp.head_base = l * H;
       cp.err = c->d_err;
+      // The mma.sync kernel has one CTA per 64 x 64 tile; when a layer has fewer tiles than two
+      // per SM (short sequences), the heads of each tile are split over more CTAs.
+      cp.head_groups = std::max(1, std::min(H, (2 * c->num_sms + std::max(c->plan_tiles, 1) - 1) /
+                                                   std::max(c->plan_tiles, 1)));
       if (use_contact_tc(c)) {
         ESM_CUDA(esm::launch_contact_tc(c->tm_qkv_q, c->tm_qkv_kv, cp, c->seq_of, s));
       } else {

@@ -124,6 +124,7 @@ struct ContactParams {
   float* r;
   int head_base;           // layer * H
   int* err;                // device error word (bounded waits of the tensor-core kernel)
+  int head_groups;         // mma.sync kernel: the contributing heads are split over this many CTAs per tile
 };
 cudaError_t launch_contact_accumulate(const ContactParams& p, cudaStream_t s);
 
