@@ -1,5 +1,6 @@
-// Bidirectional attention on tcgen05 for head_dim 64 with two score buffers per query tile, so the
-// tensor cores compute S(j + 2) while the softmax works on S(j) and S(j + 1). Same contract as
+// Bidirectional attention on tcgen05 for head_dim 64 and 32 (and 16 / 24, zero-padded to 32 by the
+// tensor maps) with two score buffers per query tile, so the tensor cores compute S(j + 2) while
+// the softmax works on S(j) and S(j + 1). Same contract as
 // attention_kernel in attention.cu (packed varlen sequences, keys past a sequence's end masked, O
 // in fp16, optional per-row log-sum-exp); replaces the reference attention loop
 // (src/lib.rs:5206-5301).
@@ -62,10 +63,14 @@ __device__ __forceinline__ uint32_t o_col(int t) { return static_cast<uint32_t>(
 // POLY of every 8 column pairs take their exponentials on the FP32 pipe (poly_exp2) instead of the
 // special-function unit. EXP selects the softmax arithmetic: 0 scalar FP32, 1 packed FP32 pairs
 // (fma/add.f32x2) and three-input maxima, 2 the same with the exponentials taken on fp16 pairs.
-template <int DH, int POLY, int EXP>
+// PAD: the heads are p.dh = 16 or 24 wide and arrive through 3-D maps ([rows][3 H][p.dh], boxes
+// 32 wide) zero-padded to DH = 32 columns, which changes neither Q K^T nor the first p.dh columns
+// of P V; only p.dh output columns are stored.
+template <int DH, int POLY, int EXP, bool PAD>
 __global__ void __launch_bounds__(kThreads3, 2)
     attention_tc3_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
                          const AttnParams p) {
+  static_assert(!PAD || DH == 32, "padded heads use the 32-column tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using G = Tc3<DH>;
@@ -116,8 +121,10 @@ __global__ void __launch_bounds__(kThreads3, 2)
       tma_prefetch_desc(&tmap_kv);
       const uint64_t pol = l2_policy_evict_normal();
       mbar_arrive_expect_tx(q_full, ntiles * kQBytes);
-      for (int t = 0; t < ntiles; ++t)
-        tma_load_2d(smem + t * kQBytes, &tmap_q, q_full, h * kD, start + q0 + t * kQ, pol);
+      for (int t = 0; t < ntiles; ++t) {
+        if constexpr (PAD) tma_load_3d(smem + t * kQBytes, &tmap_q, q_full, 0, h, start + q0 + t * kQ, pol);
+        else tma_load_2d(smem + t * kQBytes, &tmap_q, q_full, h * kD, start + q0 + t * kQ, pol);
+      }
       bool ok = true;
       int j = 0;
       for (; j < nkv; ++j) {
@@ -128,8 +135,13 @@ __global__ void __launch_bounds__(kThreads3, 2)
         }
         uint8_t* dst = smem + kOffKV + st * 2 * kKVBytes;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
-        tma_load_2d(dst, &tmap_kv, &kv_full[st], p.d + h * kD, start + j * kKV, pol);
-        tma_load_2d(dst + kKVBytes, &tmap_kv, &kv_full[st], 2 * p.d + h * kD, start + j * kKV, pol);
+        if constexpr (PAD) {
+          tma_load_3d(dst, &tmap_kv, &kv_full[st], 0, p.H + h, start + j * kKV, pol);
+          tma_load_3d(dst + kKVBytes, &tmap_kv, &kv_full[st], 0, 2 * p.H + h, start + j * kKV, pol);
+        } else {
+          tma_load_2d(dst, &tmap_kv, &kv_full[st], p.d + h * kD, start + j * kKV, pol);
+          tma_load_2d(dst + kKVBytes, &tmap_kv, &kv_full[st], 2 * p.d + h * kD, start + j * kKV, pol);
+        }
       }
       if (!ok) {  // let the copies in flight land before the CTA exits
         mbar_wait(q_full, 0, p.err, kDevTimeoutProducer);
@@ -348,7 +360,8 @@ __global__ void __launch_bounds__(kThreads3, 2)
         tc_fence_after();
         const int row = q0 + t * kQ + r;
         const float inv = 1.0f / l;
-        __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * kD;
+        const int dh_out = PAD ? p.dh : kD;  // stored columns (the padding is not part of the head)
+        __half* dst = p.out + static_cast<size_t>(start + row) * p.d + h * dh_out;
 #pragma unroll
         for (int hh = 0; hh < kD / 32; ++hh) {
           uint32_t o[32];
@@ -357,6 +370,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
           if (row < len) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
+              if (PAD && 8 * k >= dh_out) break;
               __half2 hv[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e)
@@ -377,19 +391,19 @@ __global__ void __launch_bounds__(kThreads3, 2)
   }
 }
 
-template <int DH, int POLY, int EXP>
+template <int DH, int POLY, int EXP, bool PAD = false>
 cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p, cudaStream_t s) {
   static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc3_kernel<DH, POLY, EXP>,
+    cudaError_t e = cudaFuncSetAttribute(attention_tc3_kernel<DH, POLY, EXP, PAD>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Tc3<DH>::kSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   dim3 grid(p.n_work, p.H);
-  attention_tc3_kernel<DH, POLY, EXP><<<grid, kThreads3, Tc3<DH>::kSmem, s>>>(tm_q, tm_kv32, p);
+  attention_tc3_kernel<DH, POLY, EXP, PAD><<<grid, kThreads3, Tc3<DH>::kSmem, s>>>(tm_q, tm_kv32, p);
   return cudaGetLastError();
 }
 
@@ -398,6 +412,11 @@ cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, co
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s) {
   if (p.n_work <= 0) return cudaSuccess;
+  if (p.dh == 16 || p.dh == 24) {  // zero-padded to 32 columns by the 3-D maps
+    if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1, true>(tm_q, tm_kv32, p, s)
+                                                : launch_poly3<32, 2, 1, true>(tm_q, tm_kv32, p, s);
+    return launch_poly3<32, 0, 0, true>(tm_q, tm_kv32, p, s);
+  }
   if (p.dh == 32) {  // the default arithmetic, and scalar FP32 for comparison
     if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1>(tm_q, tm_kv32, p, s)
                                                 : launch_poly3<32, 2, 1>(tm_q, tm_kv32, p, s);

@@ -108,6 +108,9 @@ struct esm_ctx {
   CUtensorMap tm_qkv_q32, tm_qkv_kv32;  // the same with 32-column boxes (head_dim 32)
   CUtensorMap tm_qkv_kv_r32;    // 64-column boxes of 32 rows (32-key K/V tiles, head_dim 64)
   CUtensorMap tm_qkv_kv32_r32;  // 32-column boxes of 32 rows, 64-byte swizzle (head_dim 32)
+  // head_dim 16 / 24: 3-D views [rows][3 H][head_dim] with 32-wide boxes of 128 / 32 rows, which
+  // zero-pad every head to 32 columns for the head_dim-32 attention tiles
+  CUtensorMap tm_qkv_hq, tm_qkv_hkv;
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
@@ -457,6 +460,10 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
             esm::make_tmap_f16_box(&c->tm_qkv_kv32, c->qkv, rows, 3 * d, 3 * d, 64, 32, 64) &&
             esm::make_tmap_f16(&c->tm_qkv_kv_r32, c->qkv, rows, 3 * d, 3 * d, 32) &&
             esm::make_tmap_f16_box(&c->tm_qkv_kv32_r32, c->qkv, rows, 3 * d, 3 * d, 32, 32, 64);
+  const int64_t dh = d / H;
+  if (ok && (dh == 16 || dh == 24))
+    ok = esm::make_tmap_f16_heads(&c->tm_qkv_hq, c->qkv, rows, 3 * H, static_cast<uint32_t>(dh), 3 * d, 128) &&
+         esm::make_tmap_f16_heads(&c->tm_qkv_hkv, c->qkv, rows, 3 * H, static_cast<uint32_t>(dh), 3 * d, 32);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -645,9 +652,11 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
-  // head_dim 64 and 32 run the tcgen05 kernel (attention_tc3.cu) unless ESM_ATTN_TC=0; head_dim
-  // 16 and 24 the mma.sync kernel (attention.cu).
-  const bool attn_tc = (dh == 64 || dh == 32) && c->attn_tc != 0;
+  // head_dim 64, 32, 24 and 16 run the tcgen05 kernel (attention_tc3.cu; 16 and 24 zero-padded to
+  // 32 by the 3-D tensor maps) unless ESM_ATTN_TC=0, which selects the mma.sync kernel
+  // (attention.cu).
+  const bool attn_tc = (dh == 64 || dh == 32 || dh == 24 || dh == 16) && c->attn_tc != 0;
+  const bool head_pad = dh == 16 || dh == 24;
   esm::AttnParams ap256 = ap;
   ap256.work = c->work256;
   ap256.n_work = c->plan_work256;
@@ -710,9 +719,9 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
       if (attn_tc) {
         const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 ? 2 : 0);
-        ESM_CUDA(esm::launch_attention_tc3(dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q,
-                                           dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32, ap256, poly, c->attn_exp,
-                                           s));
+        ESM_CUDA(esm::launch_attention_tc3(head_pad ? c->tm_qkv_hq : (dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q),
+                                           head_pad ? c->tm_qkv_hkv : (dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32),
+                                           ap256, poly, c->attn_exp, s));
       } else {
         ESM_CUDA(esm::launch_attention(ap, s));
       }

@@ -785,6 +785,23 @@ bool make_tmap_f16_box(CUtensorMap* map, const void* base, uint64_t rows, uint64
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_f16_heads(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads, uint32_t head_dim,
+                         uint64_t ld, uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr || head_dim == 0 || head_dim > 32 || ((head_dim * 2) & 15)) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15) || box_rows == 0 || box_rows > 256) return false;
+  // [rows][heads][head_dim] with a box 32 elements wide: columns head_dim..31 of every row are
+  // outside the tensor and arrive as zeros.
+  const cuuint64_t dims[3] = {head_dim, heads, rows};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim) * 2, ld * 2};
+  const cuuint32_t box[3] = {32, 1, box_rows};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr || (elem_bytes != 2 && elem_bytes != 4)) return false;

@@ -36,6 +36,12 @@ bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 // Same with an explicit box width (box_cols fp16 columns) and swizzle (64 or 128 bytes).
 bool make_tmap_f16_box(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                        uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
+// fp16 map over the heads of a [rows, ld] matrix whose columns are `heads` consecutive heads of
+// head_dim (16 or 24) elements: a 3-D view [rows][heads][head_dim] with boxes of 32 x 1 x box_rows
+// and 64-byte swizzle, so each row of a head lands in shared memory zero-padded to 32 elements
+// (the elements past head_dim are outside the tensor and the TMA fills them with zeros).
+bool make_tmap_f16_heads(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads, uint32_t head_dim,
+                         uint64_t ld, uint32_t box_rows);
 
 // Tensor map for the epilogue's bulk stores: a row-major [rows, cols] matrix of fp16 (elem_bytes 2)
 // or fp32 (4), box = [32 rows, 64 bytes], 64-byte swizzle.

@@ -459,3 +459,19 @@ def test_dequantisation_overlap_is_exact(esm, monkeypatch):
         m.close()
     for a, b in zip(outs["1"], outs["0"]):
         np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("arch,attn", [(0, "3"), (0, "0"), (1, "3"), (1, "0")])
+def test_head_dim_16_and_24_attention(esm, orc, monkeypatch, arch, attn):
+    # head_dim 16 (ESM-2 8M) and 24 (35M) on the tcgen05 kernel, fed through 3-D tensor maps that
+    # zero-pad each head to 32 columns (3), and on the mma.sync kernel (0), with contacts, on
+    # lengths around the 32-key and 128/256-row tile edges.
+    monkeypatch.setenv("ESM_ATTN_TC", attn)
+    base = esm.EsmConfig.preset(arch)
+    cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
+    m, t, cw = build(esm, cfg, esm.DTYPE_Q8_0, seed=24 + arch)
+    lens = [5, 33, 64, 65, 129, 256, 257, 511]
+    m.reserve(sum(lens), len(lens), 511, contacts=True)
+    seqs = esm.random_sequences(len(lens), lens, seed=25 + arch)
+    out = m.forward(seqs, want_hidden=True, want_contacts=True)
+    compare(orc, cfg, esm.DTYPE_Q8_0, t, seqs, out, cw)
