@@ -547,76 +547,7 @@ inline DmsPipelineResult run_pipeline_dms_with_mode(const FastaRecord& record, s
   return r;
 }
 
-// aa_category, src/ui.rs:77-89.
-inline const char* aa_category(char aa) {
-  switch (aa) {
-    case 'A': case 'V': case 'L': case 'I': case 'M': return "Hydrophobic Aliphatic";
-    case 'F': case 'W': case 'Y': return "Hydrophobic Aromatic";
-    case 'K': case 'R': case 'H': return "Basic Positively Charged";
-    case 'D': case 'E': return "Acidic Negatively Charged";
-    case 'S': case 'T': case 'N': case 'Q': return "Polar Uncharged";
-    case 'C': return "Cysteine (Disulfide / Redox)";
-    case 'G': case 'P': return "Special Conformation (Loop/Kink)";
-    case '*': return "Masked Token (<mask_1>)";
-    default: return "Non-standard Residue";
-  }
-}
-
-struct InpaintCandidate {  // src/pipeline.rs:584-588
-  char amino_acid = 0;
-  float probability_pct = 0.0f;
-  const char* category = "";
-};
-
-struct InpaintSite {  // src/pipeline.rs:592-598
-  size_t position = 0;   // token index = 1-based residue position (<cls> is token 0)
-  size_t token_idx = 0;
-  char native_char = '*';
-  char predicted_char = 0;
-  std::vector<InpaintCandidate> candidates;  // the five most likely residues
-};
-
-struct InpaintPipelineResult {  // src/pipeline.rs:602-607
-  std::string protein_id, original_sequence, reconstructed_sequence;
-  std::vector<InpaintSite> sites;
-};
-
-// compute_pipeline_inpaint_parallel (src/pipeline.rs:619-707): one forward without contacts, then
-// for every <mask> row the canonical log-softmax, the 20 residues in descending order (a stable
-// sort, so ties keep id order), the best one written into the reconstructed sequence and the top
-// five reported with exp(log p) * 100 and their category.
-inline InpaintPipelineResult compute_pipeline_inpaint_parallel(const FastaRecord& record, const EsmConfig& cfg,
-                                                               DeviceWeights& w, size_t /*num_threads*/) {
-  std::vector<size_t> tokens = Tokenizer::encode(record.sequence);
-  BidirectionalRunState state(cfg, tokens.size());
-  state.compute_contacts = false;
-  detail::run(tokens, w, state);
-  InpaintPipelineResult r;
-  r.protein_id = record.id;
-  r.original_sequence = record.sequence;
-  std::vector<size_t> rebuilt = tokens;
-  for (size_t i = 0; i < tokens.size(); ++i) {
-    if (tokens[i] != 32) continue;
-    const std::vector<float> lp = log_softmax_canonical(&state.logits[i * cfg.vocab_size]);
-    std::vector<std::pair<size_t, float>> cands;
-    for (size_t id = 4; id <= 23; ++id) cands.emplace_back(id, lp[id]);
-    std::stable_sort(cands.begin(), cands.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
-    rebuilt[i] = cands[0].first;
-    InpaintSite site;
-    site.position = site.token_idx = i;
-    site.predicted_char = Tokenizer::decode(cands[0].first);
-    for (size_t k = 0; k < 5; ++k) {
-      const char c = Tokenizer::decode(cands[k].first);
-      site.candidates.push_back({c, std::exp(cands[k].second) * 100.0f, aa_category(c)});
-    }
-    r.sites.push_back(std::move(site));
-  }
-  for (size_t i = 1; i + 1 < rebuilt.size(); ++i)
-    if (const char c = Tokenizer::decode(rebuilt[i])) r.reconstructed_sequence.push_back(c);
-  return r;
-}
-
-// The convenience forms (src/pipeline.rs:33-74, 389-407, 610-617), without the terminal theme.
+// The DMS convenience forms (src/pipeline.rs:33-74), without the terminal theme.
 inline DmsPipelineResult run_pipeline_dms_parallel(const FastaRecord& record, size_t window_size, size_t stride,
                                                    const EsmConfig& cfg, DeviceWeights& w, size_t num_threads) {
   return run_pipeline_dms_with_mode(record, window_size, stride, cfg, w, num_threads, DmsScoringMode::MaskedMarginal);
@@ -624,9 +555,6 @@ inline DmsPipelineResult run_pipeline_dms_parallel(const FastaRecord& record, si
 inline DmsPipelineResult run_pipeline_dms(const FastaRecord& record, size_t window_size, size_t stride,
                                           const EsmConfig& cfg, EsmWeights& w) {
   return run_pipeline_dms_parallel(record, window_size, stride, cfg, w, 1);
-}
-inline InpaintPipelineResult compute_pipeline_inpaint(const FastaRecord& record, const EsmConfig& cfg, EsmWeights& w) {
-  return compute_pipeline_inpaint_parallel(record, cfg, w, 1);
 }
 
 struct ContactPair {  // src/benchmark.rs:107-115

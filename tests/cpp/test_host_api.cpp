@@ -12,7 +12,7 @@
 //   test_host_api misuse <q4 file>                  the reference's panics and io errors
 //   test_host_api pipelines <fp32 file> <sequence> <out.bin>
 //                                                   load_model_weights(Q4_0), both DMS modes, the
-//                                                   contacts and inpaint pipelines, Q3_LUT blocks
+//                                                   contacts pipeline, Q3_LUT blocks
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -147,18 +147,6 @@ static void test_dms_row() {  // test_dms_row_and_csv_generation (src/export.rs:
     CHECK(std::fabs(r.mean_delta_logp - v) < 1e-5f);
     CHECK(std::string(r.category) == want);
   }
-}
-
-static void test_aa_category() {  // aa_category, src/ui.rs:77-89
-  CHECK(std::string(aa_category('L')) == "Hydrophobic Aliphatic");
-  CHECK(std::string(aa_category('W')) == "Hydrophobic Aromatic");
-  CHECK(std::string(aa_category('H')) == "Basic Positively Charged");
-  CHECK(std::string(aa_category('E')) == "Acidic Negatively Charged");
-  CHECK(std::string(aa_category('Q')) == "Polar Uncharged");
-  CHECK(std::string(aa_category('C')) == "Cysteine (Disulfide / Redox)");
-  CHECK(std::string(aa_category('P')) == "Special Conformation (Loop/Kink)");
-  CHECK(std::string(aa_category('*')) == "Masked Token (<mask_1>)");
-  CHECK(std::string(aa_category('X')) == "Non-standard Residue");
 }
 
 static void test_config_presets() {  // src/lib.rs:87-150
@@ -414,29 +402,6 @@ static void run_pipelines(const std::string& f32, const std::string& seq, const 
   f.write(reinterpret_cast<const char*>(q3.data()), 28);
   f.write(reinterpret_cast<const char*>(dq), sizeof(dq));
 
-  // compute_pipeline_inpaint_parallel on a sequence with three masks ('*' and "<mask>").
-  const std::string masked = "MKT*AYIAK*RQ<mask>ISFVKSHFSRQLEERLG";
-  const InpaintPipelineResult ip = compute_pipeline_inpaint_parallel(FastaRecord{"m", "", masked}, cfg, w, 8);
-  const std::vector<size_t> mt = Tokenizer::encode(masked);
-  CHECK(ip.sites.size() == 3 && ip.reconstructed_sequence.size() == mt.size() - 2);
-  const int32_t nsites = static_cast<int32_t>(ip.sites.size());
-  f.write(reinterpret_cast<const char*>(&nsites), 4);
-  for (const InpaintSite& site : ip.sites) {
-    CHECK(mt[site.position] == 32 && site.candidates.size() == 5);
-    CHECK(site.predicted_char == site.candidates[0].amino_acid);
-    CHECK(ip.reconstructed_sequence[site.position - 1] == site.predicted_char);
-    for (size_t k = 0; k < 5; ++k) {
-      CHECK(std::string(site.candidates[k].category) == aa_category(site.candidates[k].amino_acid));
-      if (k) CHECK(site.candidates[k].probability_pct <= site.candidates[k - 1].probability_pct);
-    }
-    const int32_t pos = static_cast<int32_t>(site.position);
-    f.write(reinterpret_cast<const char*>(&pos), 4);
-    for (const InpaintCandidate& c : site.candidates) {
-      const int32_t ch = c.amino_acid;
-      f.write(reinterpret_cast<const char*>(&ch), 4);
-    }
-    for (const InpaintCandidate& c : site.candidates) f.write(reinterpret_cast<const char*>(&c.probability_pct), 4);
-  }
 }
 
 int main(int argc, char** argv) {
@@ -454,7 +419,6 @@ int main(int argc, char** argv) {
       test_quantize_slice_rejects_ragged_length();
       test_config_presets();
       test_dms_row();
-      test_aa_category();
       test_detect_from_file_errors(argv[2]);
     } else if (cmd == "forward" && argc == 8) {
       const std::string kind = argv[3];

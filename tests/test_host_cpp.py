@@ -130,8 +130,6 @@ def test_pipelines_match_oracle(esm, orc, driver, tmp_path):
     q3 = raw[off:off + 28]
     off += 28
     q3_dq = take(64)
-    nsites = int(take(1, np.int32)[0])
-    sites = [(int(take(1, np.int32)[0]), take(5, np.int32).copy(), take(5).copy()) for _ in range(nsites)]
     assert off == raw.size
 
     tq = esm.quantize_tensors(t, esm.DTYPE_Q4_0)
@@ -154,23 +152,6 @@ def test_pipelines_match_oracle(esm, orc, driver, tmp_path):
     np.testing.assert_array_equal(pairs[:, 1], rj)
     np.testing.assert_array_equal(pairs[:, 2].view(np.float32), rs)
     assert enr == renr
-
-    # compute_pipeline_inpaint_parallel (src/pipeline.rs:619-707): the masked rows of one forward,
-    # ranked by the canonical log-softmax (stable for ties). Probabilities within the logit
-    # tolerance; identities wherever the oracle's ranking is decisive.
-    masked = "MKT*AYIAK*RQ<mask>ISFVKSHFSRQLEERLG"
-    mtoks = esm.tokenize(masked)
-    mref = orc.forward(cfg, esm.DTYPE_Q4_0, tq, mtoks)["logits"]
-    assert [p for p, _, _ in sites] == [int(i) for i in np.flatnonzero(mtoks == 32)]
-    alphabet = "LAGVSERTIDPKQNFYMHWC"  # ids 4..23
-    for pos, chars, pct in sites:
-        lp = orc.log_softmax_canonical(mref[pos])[4:24]
-        order = np.argsort(-lp, kind="stable")[:5]
-        assert np.abs(np.log(pct / 100.0) - lp[[alphabet.index(chr(c)) for c in chars]]).max() <= 4e-2
-        gaps = -np.diff(np.sort(lp)[::-1][:6])
-        for k in range(5):
-            if gaps[k] > 8e-2 and (k == 0 or gaps[k - 1] > 8e-2):
-                assert chr(chars[k]) == alphabet[order[k]]
 
     src = np.sin(np.float32(0.37) * np.arange(64, dtype=np.float32)).astype(np.float32)
     np.testing.assert_array_equal(q3, esm.quantize_q3(src))
