@@ -317,10 +317,10 @@ __global__ void __launch_bounds__(kThreads3, 2)
           for (int i = 0; i < 16; ++i) {
             float a0, a1;
             f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), c2, nm2), a0, a1);
-            const bool poly = (i & 7) < POLY;
-            const float e0 = poly ? poly_exp2(a0) : fast_exp2(a0);
-            const float e1 = poly ? poly_exp2(a1) : fast_exp2(a1);
-            rs2[i & 3] = f2_add(rs2[i & 3], f2_pack(e0, e1));
+            const uint64_t e2 = (i & 7) < POLY ? poly_exp2_x2(a0, a1) : f2_pack(fast_exp2(a0), fast_exp2(a1));
+            rs2[i & 3] = f2_add(rs2[i & 3], e2);
+            float e0, e1;
+            f2_unpack(e2, e0, e1);
             __half2 hv = __floats2half2_rn(e0, e1);
             pk[i] = *reinterpret_cast<uint32_t*>(&hv);
           }

@@ -335,6 +335,11 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 // Three-input maximum (one instruction on sm_100).
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float d;
@@ -358,6 +363,23 @@ __device__ __forceinline__ float poly_exp2(float x) {
   p = fmaf(p, f, 0.69326097f);
   p = fmaf(p, f, 0.99992806f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+// Two poly_exp2 on a packed FP32 pair: the same operations in the same order (each f32x2
+// instruction rounds both halves exactly as its scalar form), so the results are bit-identical to
+// poly_exp2(x0), poly_exp2(x1), in about half the issue slots.
+__device__ __forceinline__ uint64_t poly_exp2_x2(float x0, float x1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -120.0f), fmaxf(x1, -120.0f));
+  const uint64_t t = f2_add(x, f2_pack(12582912.0f, 12582912.0f));
+  const uint64_t j = f2_add(t, f2_pack(-12582912.0f, -12582912.0f));
+  const uint64_t f = f2_sub(x, j);
+  uint64_t p = f2_fma(f2_pack(0.055171605f, 0.055171605f), f, f2_pack(0.24261111f, 0.24261111f));
+  p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+  p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  return f2_pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
+                 __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
