@@ -36,9 +36,14 @@ struct esm_ctx {
   // Eighths of the softmax exponentials on the FP32 pipe (ESM_ATTN_POLY, 0..3); -1 = the kernel's
   // measured best (2 with packed arithmetic, 0 otherwise).
   int attn_poly = -1;
-  // Softmax arithmetic (ESM_ATTN_EXP): 0 scalar FP32, 1 packed FP32 pairs (default, measured
-  // fastest), 2 fp16-pair exponentials.
-  int attn_exp = 1;
+  // Softmax arithmetic (ESM_ATTN_EXP): 0 scalar FP32, 1 packed FP32 pairs with a row max per
+  // 32-key step, 2 fp16-pair exponentials, 3 packed FP32 pairs against the running max with the
+  // max refreshed only when a step's row sum exceeds attn_rescale_sum (default, measured fastest:
+  // about 4 % less attention time than 1 at c4).
+  int attn_exp = 3;
+  // exp_mode 3: the row-sum bound of a 32-key step above which the running max is refreshed
+  // (ESM_ATTN_RESCALE_SUM, 64 .. 32768; small values exercise the refresh path in the tests).
+  float attn_rescale_sum = 32768.0f;
   int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
   std::string err;
@@ -652,6 +657,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.dh = dh;
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
+  ap.rescale_sum = c->attn_rescale_sum;
   // head_dim 64, 32, 24 and 16 run the tcgen05 kernel (attention_tc3.cu; 16 and 24 zero-padded to
   // 32 by the 3-D tensor maps) unless ESM_ATTN_TC=0, which selects the mma.sync kernel
   // (attention.cu).
@@ -718,7 +724,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
       if (attn_tc) {
-        const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 ? 2 : 0);
+        const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 || c->attn_exp == 3 ? 2 : 0);
         ESM_CUDA(esm::launch_attention_tc3(head_pad ? c->tm_qkv_hq : (dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q),
                                            head_pad ? c->tm_qkv_hkv : (dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32),
                                            ap256, poly, c->attn_exp, s));
@@ -935,7 +941,9 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   if (const char* v = std::getenv("ESM_GEMM_CTA_PAIR")) c->cta_pair = std::atoi(v) != 0;
   if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v);
   if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(3, std::max(0, std::atoi(v)));
-  if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(2, std::max(0, std::atoi(v)));
+  if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(3, std::max(0, std::atoi(v)));
+  if (const char* v = std::getenv("ESM_ATTN_RESCALE_SUM"))
+    c->attn_rescale_sum = std::min(32768.0f, std::max(64.0f, static_cast<float>(std::atof(v))));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;
   if (const char* v = std::getenv("ESM_DEQUANT_OVERLAP")) c->deq_overlap = std::atoi(v) != 0;
   bool events_ok = cudaSetDevice(device) == cudaSuccess &&

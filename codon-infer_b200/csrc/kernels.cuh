@@ -84,6 +84,9 @@ struct AttnParams {
   int T, d, H, dh;
   float scale;             // 1/sqrt(dh)
   int* err;                // device error word (bounded waits of the tcgen05 kernel)
+  // tcgen05 kernel, exp_mode 3: a 32-key step whose row sum against the running max exceeds this
+  // (>= 64) refreshes the max; it also bounds every P value, which must stay finite in fp16.
+  float rescale_sum;
 };
 // mma.sync attention (attention.cu): work items are (sequence, 64-row query tile); any head_dim
 // that is a multiple of 8 up to 64.
@@ -100,7 +103,8 @@ cudaError_t launch_contact_rank(const float* map, int n, int min_sep, int k, uin
 // query block); two 128-row query tiles share every 32-key K/V tile and have two score buffers
 // each. tm_q: qkv map with head_dim-column boxes of 128 rows; tm_kv32: the same with 32 rows
 // (128- or 64-byte swizzle). poly_eighths (0..3) of the exponential pairs run on the FP32 pipe;
-// exp_mode: 0 scalar FP32, 1 packed FP32 pairs, 2 fp16-pair exponentials.
+// exp_mode: 0 scalar FP32, 1 packed FP32 pairs, 2 fp16-pair exponentials, 3 packed FP32 pairs
+// against the running max without a per-step row max (refreshed when the row sum says so).
 cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
                                  int poly_eighths, int exp_mode, cudaStream_t s);
 

@@ -355,12 +355,14 @@ def test_contact_kernels_agree(esm, monkeypatch):
 
 
 @pytest.mark.parametrize("attn,poly,exp", [("3", "0", "0"), ("3", "2", "0"), ("3", "3", "0"), ("3", "0", "1"),
-                                           ("3", "2", "1"), ("3", "0", "2"), ("0", "0", "0")])
+                                           ("3", "2", "1"), ("3", "0", "2"), ("3", "0", "3"), ("3", "2", "3"),
+                                           ("0", "0", "0")])
 def test_650m_shape_attention_kernels(esm, orc, monkeypatch, attn, poly, exp):
     # The tcgen05 attention kernel (ESM_ATTN_TC=3, the default: two 128-row query tiles sharing
     # 32-key K/V tiles, two score buffers per tile; ESM_ATTN_POLY eighths of the exponentials on the
     # FP32 pipe; ESM_ATTN_EXP the softmax arithmetic: scalar, packed FP32 pairs, fp16-pair
-    # exponentials) and the mma.sync kernel (ESM_ATTN_TC=0) on lengths at and around the 32-key and
+    # exponentials, packed pairs without a per-step row max) and the mma.sync kernel
+    # (ESM_ATTN_TC=0) on lengths at and around the 32-key and
     # 128/256-row tile edges, with contacts (which read the saved log-sum-exp).
     monkeypatch.setenv("ESM_ATTN_TC", attn)
     monkeypatch.setenv("ESM_ATTN_POLY", poly)
@@ -413,13 +415,19 @@ def test_150m_shape_head_dim_32_attention(esm, orc, monkeypatch, attn):
     compare(orc, cfg, esm.DTYPE_FP32, t, seqs, out, cw)
 
 
-@pytest.mark.parametrize("attn", ["3", "0"])
-def test_attention_rescale_path(esm, orc, monkeypatch, attn):
+@pytest.mark.parametrize("attn,exp,rsum", [("3", "1", None), ("3", "3", None), ("3", "3", "64"), ("0", "1", None)])
+def test_attention_rescale_path(esm, orc, monkeypatch, attn, exp, rsum):
     # Query and key weights three times larger than the other tests' give scaled scores whose row
     # maxima grow by more than 2^8 (in the exp2 domain) from one 128-key block to the next in about
     # a tenth of the rows of the 640-token sequence (counted offline from the same weights), so the
     # lazy rescale of O runs there (the 32-key tiles of the tcgen05 kernel see at least as many).
+    # With ESM_ATTN_EXP=3 the refresh is decided by a step's row sum against the stale max; with
+    # ESM_ATTN_RESCALE_SUM=64 it runs whenever that sum exceeds 64, which the growing maxima of
+    # these weights cause far more often than the default bound of 2^15.
     monkeypatch.setenv("ESM_ATTN_TC", attn)
+    monkeypatch.setenv("ESM_ATTN_EXP", exp)
+    if rsum is not None:
+        monkeypatch.setenv("ESM_ATTN_RESCALE_SUM", rsum)
     base = esm.esm2_650m()
     cfg = esm.EsmConfig(base.dim, base.hidden_dim, 2, base.n_heads, arch=base.arch)
     t32 = esm.synth_fp32_tensors(cfg, seed=14, bias_std=0.02, ln_jitter=0.1)
