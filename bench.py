@@ -4,7 +4,7 @@ Workload (default, c4): ESM-2 650M with Q4_0 weights (random-init N(0, 0.02), qu
 bit-exact BlockQ4_0 quantizer), 64 sequences x L = 1024 tokens of uniform-random residues per GPU,
 logits [64, 1024, 33] out. Metric: residues/s over the whole job (tokens incl. <cls>/<eos>).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1..c5]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|vendor] [--config c1..c5]
   torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
 
 Scaling. Forward configurations (c1, c2, c4, c5) are weak-scaled in `value`: every rank runs its
@@ -19,7 +19,8 @@ into N contiguous blocks and only the per-variant rows cross between GPUs.
 esm_dms_masked_marginal_range for the scan: host buffers in and out) with the copies inside the
 timed region. --impl reference times the CPU restatement of the reference forward (the reference
 crate is Rust and cannot be built in this image) on the host cores, one sequence per step; that
-arm loads only the oracle library.
+arm loads only the oracle library. --impl vendor times the same projections and attention with
+cuBLAS and cuDNN (a yardstick for the kernels, not a forward; see run_vendor).
 """
 from __future__ import annotations
 
@@ -482,6 +483,70 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_vendor(args):
+    """Vendor-library yardstick for the same matmul and attention work: per layer, the four
+    projections as cuBLAS fp16 GEMMs (torch.matmul, plain outputs) and the attention as cuDNN's
+    fused kernel (torch SDPA, dense [B, H, L, dh]), in forward order so that every call runs at the
+    clock a full forward gets. No embedding, LayerNorm, bias, RoPE, GELU, residual, LM head or
+    contact head, so it is a lower bound on a vendor-library forward, not one. Fixed-length
+    forward configs only (c1, c4, c5); one GPU."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    c = CONFIGS[args.config]
+    if c["dms"] or c["lengths"] != "fixed" or args.gpus != 1:
+        emit({"impl": "vendor", "unavailable": "fixed-length forward configs on one GPU only"})
+        return
+    cfg = synth.preset(c["arch"])
+    d, F_, H, nl = cfg.dim, cfg.hidden_dim, cfg.n_heads, cfg.n_layers
+    B, L = args.batch or c["batch"], c["seq_len"]
+    M, dh = B * L, d // H
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    shapes = [(3 * d, d), (d, d), (F_, d), (d, F_)]
+    A = [torch.randn(M, k, device=dev, dtype=torch.float16, generator=g) for _, k in shapes]
+    W = [torch.randn(n, k, device=dev, dtype=torch.float16, generator=g) * 0.02 for n, k in shapes]
+    q, k, v = (torch.randn(B, H, L, dh, device=dev, dtype=torch.float16, generator=g) for _ in range(3))
+
+    def events():
+        return [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nl)]
+
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def step(ev):
+        for l in range(nl):
+            e = ev[l]
+            e[0].record()
+            torch.matmul(A[0], W[0].t())
+            e[1].record()
+            F.scaled_dot_product_attention(q, k, v)
+            e[2].record()
+            for i in (1, 2, 3):
+                torch.matmul(A[i], W[i].t())
+            e[3].record()
+
+    with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+        warm = events()
+        for _ in range(args.warmup):
+            step(warm)
+        timed = [events() for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        t0.record()
+        for ev in timed:
+            step(ev)
+        t1.record()
+        torch.cuda.synchronize()
+    gemm = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for ev in timed for e in ev)
+    attn = sum(e[1].elapsed_time(e[2]) for ev in timed for e in ev)
+    ms = t0.elapsed_time(t1) / args.steps
+    emit({"impl": "vendor", "metric": metric_name(args.config, c), "value": M / (ms / 1000.0), "unit": UNIT,
+          "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+          "config": {"workload": c["desc"], "batch_per_gpu": B, "seq_len": L},
+          "parts_ms_per_step": {"gemm_cublas": gemm / args.steps, "attention_cudnn": attn / args.steps},
+          "note": "projections (cuBLAS) and attention (cuDNN) only, in forward order; no other work"})
+
+
 def main():
     # The JSON line is the only thing on stdout: everything else written to file descriptor 1
     # (library banners such as NCCL's version line at communicator set-up) goes to stderr.
@@ -493,7 +558,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "vendor"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c4",
                     help="c4 (headline, default): 650M Q4_0 64 x 1024; c1/c2/c3/c5: the other benchmark configs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -501,6 +566,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "vendor":
+        run_vendor(args)
     else:
         run_ours(args)
 
