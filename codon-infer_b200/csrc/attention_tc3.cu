@@ -40,13 +40,16 @@ constexpr int kKV = 32;   // keys per K/V tile
 constexpr int kThreads3 = 352;
 constexpr int kStages3 = 8;
 // Tile geometry for head_dim DH: 64 (128-byte rows, 128-byte swizzle) or 32 (64-byte rows and
-// swizzle). The UMMA descriptors of both layouts differ only in the high word.
-template <int DH>
+// swizzle). The UMMA descriptors of both layouts differ only in the high word. With SPLIT (the
+// zero-padded 16 / 24-wide heads) shared memory also holds the fp16 rounding residues of the two
+// query tiles and of every key tile: Q_hi t0 | Q_hi t1 | Q_lo t0 | Q_lo t1, stages K | V | K_lo.
+template <int DH, int SPLIT = 0>  // SPLIT: 0 plain scores, 2 with the query and key residues
 struct Tc3 {
   static constexpr int kQBytes = kQ * DH * 2;    // one query tile
   static constexpr int kKVBytes = kKV * DH * 2;  // one K or V tile
-  static constexpr int kOffKV = 2 * kQBytes;
-  static constexpr int kOffBar = kOffKV + kStages3 * 2 * kKVBytes;
+  static constexpr int kStageTiles = SPLIT == 2 ? 3 : 2;
+  static constexpr int kOffKV = (SPLIT ? 4 : 2) * kQBytes;
+  static constexpr int kOffBar = kOffKV + kStages3 * kStageTiles * kKVBytes;
   static constexpr int kSmem = kOffBar + 256 + 1024;
   static constexpr uint32_t kDescHi = DH == 64 ? kSw128DescHi : kSw64DescHi;
 };
@@ -68,15 +71,22 @@ __device__ __forceinline__ uint32_t o_col(int t) { return static_cast<uint32_t>(
 // when the max is refreshed).
 // PAD: the heads are p.dh = 16 or 24 wide and arrive through 3-D maps ([rows][3 H][p.dh], boxes
 // 32 wide) zero-padded to DH = 32 columns, which changes neither Q K^T nor the first p.dh columns
-// of P V; only p.dh output columns are stored.
-template <int DH, int POLY, int EXP, bool PAD>
+// of P V; only p.dh output columns are stored. These heads also take their scores in split
+// precision: tmap_qlo / tmap_klo read the fp16 rounding residues of the queries and keys
+// ([rows][2 H][p.dh], written by the QKV projection) and S = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T,
+// which leaves only the products of two residues out of the fp32 score. (With peaked attention,
+// as in trained models, fp16 queries and keys alone move the scores of the dominant keys by a few
+// hundredths and the logits by about 1e-2.) Other head sizes pass tmap_q / tmap_kv again there.
+template <int DH, int POLY, int EXP, bool PAD, int SPLIT>
 __global__ void __launch_bounds__(kThreads3, 2)
     attention_tc3_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
+                         const __grid_constant__ CUtensorMap tmap_qlo, const __grid_constant__ CUtensorMap tmap_klo,
                          const AttnParams p) {
   static_assert(!PAD || DH == 32, "padded heads use the 32-column tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  using G = Tc3<DH>;
+  static_assert(SPLIT == (PAD ? 2 : 0), "the padded heads, and only they, take split scores");
+  using G = Tc3<DH, SPLIT>;
   constexpr int kD = DH, kQBytes = G::kQBytes, kKVBytes = G::kKVBytes, kOffKV = G::kOffKV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kOffBar);
   uint64_t* q_full = bars + 0;
@@ -123,10 +133,15 @@ __global__ void __launch_bounds__(kThreads3, 2)
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_kv);
       const uint64_t pol = l2_policy_evict_normal();
-      mbar_arrive_expect_tx(q_full, ntiles * kQBytes);
+      mbar_arrive_expect_tx(q_full, ntiles * kQBytes * (SPLIT ? 2 : 1));
       for (int t = 0; t < ntiles; ++t) {
-        if constexpr (PAD) tma_load_3d(smem + t * kQBytes, &tmap_q, q_full, 0, h, start + q0 + t * kQ, pol);
-        else tma_load_2d(smem + t * kQBytes, &tmap_q, q_full, h * kD, start + q0 + t * kQ, pol);
+        if constexpr (PAD) {
+          tma_load_3d(smem + t * kQBytes, &tmap_q, q_full, 0, h, start + q0 + t * kQ, pol);
+          if constexpr (SPLIT > 0)
+            tma_load_3d(smem + (2 + t) * kQBytes, &tmap_qlo, q_full, 0, h, start + q0 + t * kQ, pol);
+        } else {
+          tma_load_2d(smem + t * kQBytes, &tmap_q, q_full, h * kD, start + q0 + t * kQ, pol);
+        }
       }
       bool ok = true;
       int j = 0;
@@ -136,11 +151,13 @@ __global__ void __launch_bounds__(kThreads3, 2)
           ok = false;
           break;
         }
-        uint8_t* dst = smem + kOffKV + st * 2 * kKVBytes;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kKVBytes);
+        uint8_t* dst = smem + kOffKV + st * G::kStageTiles * kKVBytes;
+        mbar_arrive_expect_tx(&kv_full[st], G::kStageTiles * kKVBytes);
         if constexpr (PAD) {
           tma_load_3d(dst, &tmap_kv, &kv_full[st], 0, p.H + h, start + j * kKV, pol);
           tma_load_3d(dst + kKVBytes, &tmap_kv, &kv_full[st], 0, 2 * p.H + h, start + j * kKV, pol);
+          if constexpr (SPLIT == 2)
+            tma_load_3d(dst + 2 * kKVBytes, &tmap_klo, &kv_full[st], 0, p.H + h, start + j * kKV, pol);
         } else {
           tma_load_2d(dst, &tmap_kv, &kv_full[st], p.d + h * kD, start + j * kKV, pol);
           tma_load_2d(dst + kKVBytes, &tmap_kv, &kv_full[st], 2 * p.d + h * kD, start + j * kKV, pol);
@@ -164,7 +181,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
     if (t < ntiles && elect_one_sync()) {
       constexpr uint32_t idesc_qk = umma_idesc_f16(kQ, kKV);
       constexpr uint32_t idesc_pv = umma_idesc_f16(kQ, kD) | (1u << 16);  // B (V) is MN-major
-      constexpr uint32_t kStageLo = (2 * kKVBytes) >> 4, kVLo = kKVBytes >> 4, kQLo = kQBytes >> 4;
+      constexpr uint32_t kStageLo = (G::kStageTiles * kKVBytes) >> 4, kVLo = kKVBytes >> 4, kQLo = kQBytes >> 4;
       constexpr uint32_t kVStepLo = (16 * kD * 2) >> 4;  // 16 keys of V
       const uint32_t q_lo = umma_sw128_lo(smem_u32(smem)) + t * kQLo;
       const uint32_t kv_lo = umma_sw128_lo(smem_u32(smem + kOffKV));
@@ -176,10 +193,17 @@ __global__ void __launch_bounds__(kThreads3, 2)
         const uint32_t b = kv_lo + (j % kStages3) * kStageLo;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) umma_f16_lo<G::kDescHi>(d, q_lo + 2 * k, b + 2 * k, idesc_qk, k);
+        if constexpr (SPLIT == 2) {  // + Q_lo K_hi^T + Q_hi K_lo^T
+#pragma unroll
+          for (int k = 0; k < kD / 16; ++k) {
+            umma_f16_lo<G::kDescHi>(d, q_lo + 2 * kQLo + 2 * k, b + 2 * k, idesc_qk, 1u);
+            umma_f16_lo<G::kDescHi>(d, q_lo + 2 * k, b + 2 * kVLo + 2 * k, idesc_qk, 1u);
+          }
+        }
       };
-      bool ok = mbar_wait_spin(q_full, 0, p.err, kDevTimeoutMma);
+      bool ok = mbar_wait_hint(q_full, 0, p.err, kDevTimeoutMma, p.wait_mma_ns);
       for (int j = 0; j < 2 && j < nkv && ok; ++j) {
-        if (!mbar_wait_spin(&kv_full[j], 0, p.err, kDevTimeoutMma)) {
+        if (!mbar_wait_hint(&kv_full[j], 0, p.err, kDevTimeoutMma, p.wait_mma_ns)) {
           ok = false;
           break;
         }
@@ -189,7 +213,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
       }
       for (int j = 0; j < nkv && ok; ++j) {
         const int bj = j & 1;
-        if (!mbar_wait_spin(&p_full[2 * t + bj], (j >> 1) & 1, p.err, kDevTimeoutMma)) {
+        if (!mbar_wait_hint(&p_full[2 * t + bj], (j >> 1) & 1, p.err, kDevTimeoutMma, p.wait_mma_ns)) {
           ok = false;
           break;
         }
@@ -202,7 +226,8 @@ __global__ void __launch_bounds__(kThreads3, 2)
                                      (j > 0 || k > 0) ? 1u : 0u);
         umma_commit_addr(bar_e + 8 * (j % kStages3));
         if (j + 2 < nkv) {
-          if (!mbar_wait_spin(&kv_full[(j + 2) % kStages3], ((j + 2) / kStages3) & 1, p.err, kDevTimeoutMma)) {
+          if (!mbar_wait_hint(&kv_full[(j + 2) % kStages3], ((j + 2) / kStages3) & 1, p.err, kDevTimeoutMma,
+                              p.wait_mma_ns)) {
             ok = false;
             break;
           }
@@ -476,63 +501,66 @@ __global__ void __launch_bounds__(kThreads3, 2)
   }
 }
 
-template <int DH, int POLY, int EXP, bool PAD = false>
-cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p, cudaStream_t s) {
+template <int DH, int POLY, int EXP, bool PAD = false, int SPLIT = PAD ? 2 : 0>
+cudaError_t launch_poly3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const CUtensorMap& tm_qlo,
+                         const CUtensorMap& tm_klo, const AttnParams& p, cudaStream_t s) {
   static std::atomic<unsigned long long> configured{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(configured.load(std::memory_order_acquire) & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc3_kernel<DH, POLY, EXP, PAD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Tc3<DH>::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(attention_tc3_kernel<DH, POLY, EXP, PAD, SPLIT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Tc3<DH, SPLIT>::kSmem);
     if (e != cudaSuccess) return e;
     if (dev < 64) configured.fetch_or(1ull << dev, std::memory_order_release);
   }
   dim3 grid(p.n_work, p.H);
-  attention_tc3_kernel<DH, POLY, EXP, PAD><<<grid, kThreads3, Tc3<DH>::kSmem, s>>>(tm_q, tm_kv32, p);
+  attention_tc3_kernel<DH, POLY, EXP, PAD, SPLIT><<<grid, kThreads3, Tc3<DH, SPLIT>::kSmem, s>>>(tm_q, tm_kv32, tm_qlo,
+                                                                                                tm_klo, p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
-                                 int poly_eighths, int exp_mode, cudaStream_t s) {
+cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const CUtensorMap& tm_qlo,
+                                 const CUtensorMap& tm_klo, const AttnParams& p, int poly_eighths, int exp_mode,
+                                 cudaStream_t s) {
   if (p.n_work <= 0) return cudaSuccess;
   if (p.dh == 16 || p.dh == 24) {  // zero-padded to 32 columns by the 3-D maps
-    if (exp_mode == 3) return poly_eighths == 0 ? launch_poly3<32, 0, 3, true>(tm_q, tm_kv32, p, s)
-                                                : launch_poly3<32, 2, 3, true>(tm_q, tm_kv32, p, s);
-    if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1, true>(tm_q, tm_kv32, p, s)
-                                                : launch_poly3<32, 2, 1, true>(tm_q, tm_kv32, p, s);
-    return launch_poly3<32, 0, 0, true>(tm_q, tm_kv32, p, s);
+    if (exp_mode == 3) return poly_eighths == 0 ? launch_poly3<32, 0, 3, true>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s)
+                                                : launch_poly3<32, 2, 3, true>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+    if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1, true>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s)
+                                                : launch_poly3<32, 2, 1, true>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+    return launch_poly3<32, 0, 0, true>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
   }
   if (p.dh == 32) {  // the default arithmetic, and scalar FP32 for comparison
-    if (exp_mode == 3) return poly_eighths == 0 ? launch_poly3<32, 0, 3>(tm_q, tm_kv32, p, s)
-                                                : launch_poly3<32, 2, 3>(tm_q, tm_kv32, p, s);
-    if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1>(tm_q, tm_kv32, p, s)
-                                                : launch_poly3<32, 2, 1>(tm_q, tm_kv32, p, s);
-    return launch_poly3<32, 0, 0>(tm_q, tm_kv32, p, s);
+    if (exp_mode == 3) return poly_eighths == 0 ? launch_poly3<32, 0, 3>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s)
+                                                : launch_poly3<32, 2, 3>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+    if (exp_mode == 1) return poly_eighths == 0 ? launch_poly3<32, 0, 1>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s)
+                                                : launch_poly3<32, 2, 1>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+    return launch_poly3<32, 0, 0>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
   }
   if (p.dh != 64) return cudaErrorInvalidValue;
-  if (exp_mode == 2) return launch_poly3<64, 0, 2>(tm_q, tm_kv32, p, s);
+  if (exp_mode == 2) return launch_poly3<64, 0, 2>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
   if (exp_mode == 3) {
     switch (poly_eighths) {
-      case 0: return launch_poly3<64, 0, 3>(tm_q, tm_kv32, p, s);
-      case 1: return launch_poly3<64, 1, 3>(tm_q, tm_kv32, p, s);
-      case 2: return launch_poly3<64, 2, 3>(tm_q, tm_kv32, p, s);
-      default: return launch_poly3<64, 3, 3>(tm_q, tm_kv32, p, s);
+      case 0: return launch_poly3<64, 0, 3>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+      case 1: return launch_poly3<64, 1, 3>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+      case 2: return launch_poly3<64, 2, 3>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+      default: return launch_poly3<64, 3, 3>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
     }
   }
   if (exp_mode == 1) {
     switch (poly_eighths) {
-      case 0: return launch_poly3<64, 0, 1>(tm_q, tm_kv32, p, s);
-      case 1: return launch_poly3<64, 1, 1>(tm_q, tm_kv32, p, s);
-      case 2: return launch_poly3<64, 2, 1>(tm_q, tm_kv32, p, s);
-      default: return launch_poly3<64, 3, 1>(tm_q, tm_kv32, p, s);
+      case 0: return launch_poly3<64, 0, 1>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+      case 1: return launch_poly3<64, 1, 1>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+      case 2: return launch_poly3<64, 2, 1>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+      default: return launch_poly3<64, 3, 1>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
     }
   }
   switch (poly_eighths) {
-    case 0: return launch_poly3<64, 0, 0>(tm_q, tm_kv32, p, s);
-    case 1: return launch_poly3<64, 1, 0>(tm_q, tm_kv32, p, s);
-    default: return launch_poly3<64, 2, 0>(tm_q, tm_kv32, p, s);
+    case 0: return launch_poly3<64, 0, 0>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+    case 1: return launch_poly3<64, 1, 0>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
+    default: return launch_poly3<64, 2, 0>(tm_q, tm_kv32, tm_qlo, tm_klo, p, s);
   }
 }
 

@@ -117,6 +117,35 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, i
                                                uint64_t limit_ns = kWaitLimitNs) {
   return mbar_wait_t<false>(bar, parity, err, code, limit_ns);
 }
+// With a short suspension (hint_ns > 0): the thread sleeps at most hint_ns per try, so a waiting
+// warp takes few issue slots from its sub-partition and still resumes within about hint_ns of the
+// phase completing. hint_ns == 0 is mbar_wait_spin.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_hint(uint64_t* bar, uint32_t parity, int* err, int code, uint32_t hint_ns,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+  if (hint_ns == 0) return mbar_wait_t<false>(bar, parity, err, code, limit_ns);
+  if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(err, code);
+      return false;
+    }
+  }
+}
 
 // ---- TMA ----------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -44,6 +44,9 @@ struct esm_ctx {
   // exp_mode 3: the row-sum bound of a 32-key step above which the running max is refreshed
   // (ESM_ATTN_RESCALE_SUM, 64 .. 32768; small values exercise the refresh path in the tests).
   float attn_rescale_sum = 32768.0f;
+  // Suspension hint (ns) of the tcgen05 attention kernel's MMA-issuer waits (ESM_ATTN_WAIT_MMA;
+  // 0 = spin). 64 ns measured about 2 % less attention time than spinning at c4; 256 ns was slower.
+  uint32_t attn_wait_mma = 64;
   int contact_tc = 1;  // tcgen05 contact accumulation for head_dim 64 (ESM_CONTACT_TC=0: mma.sync kernel)
   std::mutex mu;
   std::string err;
@@ -87,6 +90,9 @@ struct esm_ctx {
   float* x = nullptr;
   __half* xn = nullptr;
   __half* qkv = nullptr;
+  // head_dim 16 / 24: fp16 rounding residues of the rotated queries and keys, [rows][2 d] (queries
+  // then keys, per head as in qkv), for the attention's split-precision scores
+  __half* qk_lo = nullptr;
   __half* ao = nullptr;
   __half* hb = nullptr;
   float* headf = nullptr;
@@ -116,6 +122,7 @@ struct esm_ctx {
   // head_dim 16 / 24: 3-D views [rows][3 H][head_dim] with 32-wide boxes of 128 / 32 rows, which
   // zero-pad every head to 32 columns for the head_dim-32 attention tiles
   CUtensorMap tm_qkv_hq, tm_qkv_hkv;
+  CUtensorMap tm_lo_q, tm_lo_k;  // the same views of qk_lo ([rows][2 H][head_dim])
   // pinned staging of the per-call plan, and the event that says it may be rewritten
   int32_t* h_cu = nullptr;
   int2* h_work = nullptr;
@@ -415,6 +422,8 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   A(&c->x, rows * d);
   A(&c->xn, rows * d);
   A(&c->qkv, rows * 3 * d);
+  const bool small_heads = d / H == 16 || d / H == 24;
+  if (small_heads) A(&c->qk_lo, rows * 2 * d);
   A(&c->ao, rows * d);
   A(&c->hb, rows * F);
   A(&c->headf, rows * d);
@@ -445,6 +454,7 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   ESM_CUDA(cudaMemsetAsync(c->xn, 0, rows * d * 2, c->stream));
   ESM_CUDA(cudaMemsetAsync(c->ao, 0, rows * d * 2, c->stream));
   ESM_CUDA(cudaMemsetAsync(c->hb, 0, rows * F * 2, c->stream));
+  if (small_heads) ESM_CUDA(cudaMemsetAsync(c->qk_lo, 0, rows * 2 * d * 2, c->stream));
   {
     std::vector<float2> rt = rope_table(max_len, static_cast<int>(d / H));
     ESM_CUDA(cudaMemcpyAsync(c->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, c->stream));
@@ -468,7 +478,9 @@ int reserve_impl(esm_ctx* c, int max_tokens, int max_seqs, int max_len, bool con
   const int64_t dh = d / H;
   if (ok && (dh == 16 || dh == 24))
     ok = esm::make_tmap_f16_heads(&c->tm_qkv_hq, c->qkv, rows, 3 * H, static_cast<uint32_t>(dh), 3 * d, 128) &&
-         esm::make_tmap_f16_heads(&c->tm_qkv_hkv, c->qkv, rows, 3 * H, static_cast<uint32_t>(dh), 3 * d, 32);
+         esm::make_tmap_f16_heads(&c->tm_qkv_hkv, c->qkv, rows, 3 * H, static_cast<uint32_t>(dh), 3 * d, 32) &&
+         esm::make_tmap_f16_heads(&c->tm_lo_q, c->qk_lo, rows, 2 * H, static_cast<uint32_t>(dh), 2 * d, 128) &&
+         esm::make_tmap_f16_heads(&c->tm_lo_k, c->qk_lo, rows, 2 * H, static_cast<uint32_t>(dh), 2 * d, 32);
   if (!ok) return fail(c, ESM_ECUDA, "cuTensorMapEncodeTiled failed for an activation buffer");
   c->cap_tokens = max_tokens;
   c->cap_seqs = max_seqs;
@@ -543,7 +555,7 @@ int upload_plan(esm_ctx* c, const int32_t* h_cu, int B, bool contacts, cudaStrea
 }
 
 int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap* tout, int bn, int epi, int M,
-         int N, int K, const float* bias, void* out, int ldo, cudaStream_t s) {
+         int N, int K, const float* bias, void* out, int ldo, cudaStream_t s, __half* lo = nullptr) {
   esm::GemmParams p{};
   p.M = M;
   p.N = N;
@@ -555,6 +567,8 @@ int gemm(esm_ctx* c, const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   p.rope = c->rope;
   p.rope_cols = 2 * c->cfg.dim;
   p.err = c->d_err;
+  p.lo = lo;
+  p.lo_ld = 2 * c->cfg.dim;
   const int dh = c->cfg.dim / c->cfg.n_heads;
   ESM_CUDA(esm::gemm_launch(ta, tb, tout, bn, epi, epi == esm::kEpiQkvRope ? dh : 0, p, c->num_sms, s, c->cta_pair));
   return ESM_OK;
@@ -658,6 +672,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
   ap.scale = 1.0f / std::sqrt(static_cast<float>(dh));
   ap.err = c->d_err;
   ap.rescale_sum = c->attn_rescale_sum;
+  ap.wait_mma_ns = c->attn_wait_mma;
   // head_dim 64, 32, 24 and 16 run the tcgen05 kernel (attention_tc3.cu; 16 and 24 zero-padded to
   // 32 by the 3-D tensor maps) unless ESM_ATTN_TC=0, which selects the mma.sync kernel
   // (attention.cu).
@@ -718,16 +733,17 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
     {
       ProfScope ps(c, s, ESM_PROF_GEMM, 2.0 * T * 3.0 * d * d, 0.0);
       rc = gemm(c, c->tm_xn, c->tm_wqkv[wb], out_qkv, c->bn_qkv, esm::kEpiQkvRope, T, 3 * d, d,
-                c->bqkv + static_cast<int64_t>(l) * 3 * d, c->qkv, 3 * d, s);
+                c->bqkv + static_cast<int64_t>(l) * 3 * d, c->qkv, 3 * d, s, c->qk_lo);
       if (rc) return rc;
     }
     {
       ProfScope ps(c, s, ESM_PROF_ATTENTION, 4.0 * static_cast<double>(attn_pairs) * d, 0.0);
       if (attn_tc) {
         const int poly = c->attn_poly >= 0 ? c->attn_poly : (c->attn_exp == 1 || c->attn_exp == 3 ? 2 : 0);
-        ESM_CUDA(esm::launch_attention_tc3(head_pad ? c->tm_qkv_hq : (dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q),
-                                           head_pad ? c->tm_qkv_hkv : (dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32),
-                                           ap256, poly, c->attn_exp, s));
+        const CUtensorMap& tq = head_pad ? c->tm_qkv_hq : (dh == 32 ? c->tm_qkv_q32 : c->tm_qkv_q);
+        const CUtensorMap& tkv = head_pad ? c->tm_qkv_hkv : (dh == 32 ? c->tm_qkv_kv32_r32 : c->tm_qkv_kv_r32);
+        ESM_CUDA(esm::launch_attention_tc3(tq, tkv, head_pad ? c->tm_lo_q : tq, head_pad ? c->tm_lo_k : tkv, ap256,
+                                           poly, c->attn_exp, s));
       } else {
         ESM_CUDA(esm::launch_attention(ap, s));
       }
@@ -942,6 +958,8 @@ int esm_ctx_create(int32_t device, esm_ctx** out) {
   if (const char* v = std::getenv("ESM_ATTN_TC")) c->attn_tc = std::atoi(v);
   if (const char* v = std::getenv("ESM_ATTN_POLY")) c->attn_poly = std::min(3, std::max(0, std::atoi(v)));
   if (const char* v = std::getenv("ESM_ATTN_EXP")) c->attn_exp = std::min(3, std::max(0, std::atoi(v)));
+  if (const char* v = std::getenv("ESM_ATTN_WAIT_MMA"))
+    c->attn_wait_mma = static_cast<uint32_t>(std::min(1000000, std::max(0, std::atoi(v))));
   if (const char* v = std::getenv("ESM_ATTN_RESCALE_SUM"))
     c->attn_rescale_sum = std::min(32768.0f, std::max(64.0f, static_cast<float>(std::atof(v))));
   if (const char* v = std::getenv("ESM_CONTACT_TC")) c->contact_tc = std::atoi(v) != 0;

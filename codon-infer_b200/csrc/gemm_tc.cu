@@ -570,6 +570,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             __half* dst = static_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + n;
 #pragma unroll
             for (int i = 0; i < DH / 8; ++i) store_f16x8(dst + 8 * i, v + 8 * i);
+            if (p.lo && n < p.rope_cols) {
+              // Queries and keys also keep what fp16 rounding dropped, so that attention can form
+              // its scores as q_hi k_hi + q_lo k_hi + q_hi k_lo, close to the fp32 product.
+#pragma unroll
+              for (int i = 0; i < DH; ++i) v[i] -= __half2float(__float2half_rn(v[i]));
+              __half* lo = p.lo + static_cast<size_t>(m) * p.lo_ld + n;
+#pragma unroll
+              for (int i = 0; i < DH / 8; ++i) store_f16x8(lo + 8 * i, v + 8 * i);
+            }
           }
         }
       } else if constexpr (EPI == kEpiResidF32) {

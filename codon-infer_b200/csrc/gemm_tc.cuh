@@ -26,6 +26,10 @@ struct GemmParams {
   const float2* rope;   // [max_pos, dh/2] (cos, sin) in f32 (kEpiQkvRope)
   int rope_cols;        // columns [0, rope_cols) are rotated (kEpiQkvRope)
   int* err;             // device error word
+  // kEpiQkvRope with head_dim 16 / 24, optional: the rounding residue v - fp16(v) of every rotated
+  // (query and key) column, as fp16, at lo[m * lo_ld + n] for n < rope_cols.
+  __half* lo;
+  int lo_ld;
 };
 
 // Encodes a 2-D fp16 tensor map over a row-major [rows, cols] matrix with `ld` elements per row,

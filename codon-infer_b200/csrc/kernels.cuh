@@ -87,6 +87,9 @@ struct AttnParams {
   // tcgen05 kernel, exp_mode 3: a 32-key step whose row sum against the running max exceeds this
   // (>= 64) refreshes the max; it also bounds every P value, which must stay finite in fp16.
   float rescale_sum;
+  // tcgen05 kernel: suspension hint (ns, 0 = spin) of the MMA issuers' waits, so that the issuers
+  // take few issue slots from the softmax warps that share their sub-partitions.
+  uint32_t wait_mma_ns;
 };
 // mma.sync attention (attention.cu): work items are (sequence, 64-row query tile); any head_dim
 // that is a multiple of 8 up to 64.
@@ -105,8 +108,12 @@ cudaError_t launch_contact_rank(const float* map, int n, int min_sep, int k, uin
 // (128- or 64-byte swizzle). poly_eighths (0..3) of the exponential pairs run on the FP32 pipe;
 // exp_mode: 0 scalar FP32, 1 packed FP32 pairs, 2 fp16-pair exponentials, 3 packed FP32 pairs
 // against the running max without a per-step row max (refreshed when the row sum says so).
-cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const AttnParams& p,
-                                 int poly_eighths, int exp_mode, cudaStream_t s);
+// head_dim 16 / 24 (zero-padded to 32): tm_qlo / tm_klo map the fp16 rounding residues of the
+// queries and keys ([rows][2 H][head_dim], 128- and 32-row boxes) for split-precision scores; for
+// the other head sizes they are not read (pass tm_q / tm_kv32).
+cudaError_t launch_attention_tc3(const CUtensorMap& tm_q, const CUtensorMap& tm_kv32, const CUtensorMap& tm_qlo,
+                                 const CUtensorMap& tm_klo, const AttnParams& p, int poly_eighths, int exp_mode,
+                                 cudaStream_t s);
 
 
 // Contact mode of the attention (per layer): for each head with a non-zero regression weight w,
