@@ -554,17 +554,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           if (row_ok) {
             const int n = n0 + c;
+            // Bias and (cos, sin) rows as float4: n * 4 and pos * HALF * 8 bytes are multiples of
+            // 16 for head_dim 16 and 24.
             float v[DH];
+            if (p.bias) {
+              float4 b4[DH / 4];
 #pragma unroll
-            for (int i = 0; i < DH; ++i) v[i] = __uint_as_float(r[i]) + (p.bias ? __ldg(p.bias + n + i) : 0.0f);
+              for (int i = 0; i < DH / 4; ++i) b4[i] = __ldg(reinterpret_cast<const float4*>(p.bias + n) + i);
+              const float* bb = reinterpret_cast<const float*>(b4);
+#pragma unroll
+              for (int i = 0; i < DH; ++i) v[i] = __uint_as_float(r[i]) + bb[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < DH; ++i) v[i] = __uint_as_float(r[i]);
+            }
             if (n < p.rope_cols) {
-              const float2* tab = p.rope + static_cast<size_t>(pos) * HALF;
+              float4 cs4[HALF / 2];
+              const float4* tab = reinterpret_cast<const float4*>(p.rope + static_cast<size_t>(pos) * HALF);
+#pragma unroll
+              for (int i = 0; i < HALF / 2; ++i) cs4[i] = __ldg(tab + i);
+              const float* cc = reinterpret_cast<const float*>(cs4);  // (cos, sin) pairs
 #pragma unroll
               for (int j = 0; j < HALF; ++j) {
-                const float2 cs = __ldg(tab + j);
                 const float x0 = v[j], x1 = v[j + HALF];
-                v[j] = x0 * cs.x - x1 * cs.y;
-                v[j + HALF] = x1 * cs.x + x0 * cs.y;
+                v[j] = x0 * cc[2 * j] - x1 * cc[2 * j + 1];
+                v[j + HALF] = x1 * cc[2 * j] + x0 * cc[2 * j + 1];
               }
             }
             __half* dst = static_cast<__half*>(p.out) + static_cast<size_t>(m) * p.ldo + n;
