@@ -89,13 +89,15 @@ __device__ __forceinline__ void zero_pad_cols(__half* s, int ntiles, int tid, in
   }
 }
 
-// S(16 x 64) = Q(16 x DHP) . K(64 x DHP)^T for this warp's 16 rows.
-template <int DH>
+// S(16 x 64) = Q(16 x DHP) . K(64 x DHP)^T for this warp's 16 rows (ACC: S += instead).
+template <int DH, bool ACC = false>
 __device__ __forceinline__ void qk_tile(float (&s)[8][4], const uint32_t (&qf)[AttnShape<DH>::kDHP / 16][4],
                                         const __half* sK, int lane) {
   using S = AttnShape<DH>;
+  if constexpr (!ACC) {
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+    for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+  }
 #pragma unroll
   for (int ks = 0; ks < S::kDHP / 16; ++ks) {
 #pragma unroll
@@ -247,6 +249,14 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
   constexpr int DHP = S::kDHP;
   __shared__ __align__(16) __half sQ[2][S::kTile];
   __shared__ __align__(16) __half sK[2][S::kTile];
+  // With p.qk_lo, the fp16 rounding residues of the same query and key rows: the scores are then
+  // Q K^T + Q_lo K^T + Q K_lo^T, as in the tcgen05 attention kernel whose log-sum-exp normalises
+  // them here.
+  constexpr bool kResidues = DH == 16 || DH == 24;  // the head sizes whose attention splits its scores
+  constexpr int kLoTile = kResidues ? S::kTile : 8;
+  __shared__ __align__(16) __half sQl[2][kLoTile];
+  __shared__ __align__(16) __half sKl[2][kLoTile];
+  const bool split = kResidues && p.qk_lo != nullptr;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 tl = p.tiles[blockIdx.x];
@@ -259,7 +269,28 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
 
   zero_pad_cols<DH>(&sQ[0][0], 2, tid, 128);
   zero_pad_cols<DH>(&sK[0][0], 2, tid, 128);
+  if constexpr (kResidues) {
+    if (split) {
+      zero_pad_cols<DH>(&sQl[0][0], 2, tid, 128);
+      zero_pad_cols<DH>(&sKl[0][0], 2, tid, 128);
+    }
+  }
   __syncthreads();
+  const int ld_lo = 2 * p.d;
+  // Queries and keys of head h (and their residues) for rows i0.. and j0.. into buffer `buf`.
+  auto load_tiles = [&](int h, int buf) {
+    const __half* Qg = p.qkv + static_cast<size_t>(start) * ld + h * DH;
+    load_head_tile<DH>(sQ[buf], Qg, i0, len, ld, tid, 128);
+    load_head_tile<DH>(sK[buf], Qg + p.d, j0, len, ld, tid, 128);
+    if constexpr (kResidues) {
+      if (split) {
+        const __half* Lg = p.qk_lo + static_cast<size_t>(start) * ld_lo + h * DH;
+        load_head_tile<DH>(sQl[buf], Lg, i0, len, ld_lo, tid, 128);
+        load_head_tile<DH>(sKl[buf], Lg + p.d, j0, len, ld_lo, tid, 128);
+      }
+    }
+    cp_async_commit();
+  };
 
   // Heads that contribute (non-zero regression weight), up to 64; with several CTAs per tile
   // (gridDim.y = head groups, when a layer has too few tiles to fill the GPU) this CTA takes every
@@ -274,22 +305,14 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
   for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
 
   if (nh > 0) {
-    {
-      const __half* Qg = p.qkv + static_cast<size_t>(start) * ld + heads[0] * DH;
-      load_head_tile<DH>(sQ[0], Qg, i0, len, ld, tid, 128);
-      load_head_tile<DH>(sK[0], Qg + p.d, j0, len, ld, tid, 128);
-      cp_async_commit();
-    }
+    load_tiles(heads[0], 0);
     const int g = lane >> 2;
     const int row_a = i0 + warp * 16 + g;  // token rows held by this thread (and row_a + 8)
     for (int t = 0; t < nh; ++t) {
       const int h = heads[t];
       const int buf = t & 1;
       if (t + 1 < nh) {
-        const __half* Qg = p.qkv + static_cast<size_t>(start) * ld + heads[t + 1] * DH;
-        load_head_tile<DH>(sQ[buf ^ 1], Qg, i0, len, ld, tid, 128);
-        load_head_tile<DH>(sK[buf ^ 1], Qg + p.d, j0, len, ld, tid, 128);
-        cp_async_commit();
+        load_tiles(heads[t + 1], buf ^ 1);
         cp_async_wait<1>();
       } else {
         cp_async_wait<0>();
@@ -301,6 +324,15 @@ __global__ void __launch_bounds__(128) contact_accumulate_kernel(const ContactPa
         ldmatrix_x4(qf[ks], sQ[buf] + (warp * 16 + (lane & 15)) * S::kStr + ks * 16 + (lane >> 4) * 8);
       float s[8][4];
       qk_tile<DH>(s, qf, sK[buf], lane);
+      if constexpr (kResidues) {
+        if (split) {
+          qk_tile<DH, true>(s, qf, sKl[buf], lane);  // + Q K_lo^T
+#pragma unroll
+          for (int ks = 0; ks < DHP / 16; ++ks)
+            ldmatrix_x4(qf[ks], sQl[buf] + (warp * 16 + (lane & 15)) * S::kStr + ks * 16 + (lane >> 4) * 8);
+          qk_tile<DH, true>(s, qf, sK[buf], lane);  // + Q_lo K^T
+        }
+      }
 
       const float w = p.w_layer[h];
       const float* lse = p.lse + static_cast<size_t>(h) * p.T + start;

@@ -761,6 +761,7 @@ int forward_impl(esm_ctx* c, const int32_t* d_tokens, const int32_t* h_cu, int B
       cp.H = H;
       cp.dh = dh;
       cp.scale = ap.scale;
+      cp.qk_lo = (head_pad && attn_tc) ? c->qk_lo : nullptr;  // the scores the log-sum-exp came from
       cp.w_layer = c->d_ch_w + static_cast<int64_t>(l) * H;
       cp.m_off = c->m_off;
       cp.M = c->M;

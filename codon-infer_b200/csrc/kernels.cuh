@@ -136,6 +136,7 @@ struct ContactParams {
   int head_base;           // layer * H
   int* err;                // device error word (bounded waits of the tensor-core kernel)
   int head_groups;         // mma.sync kernel: the contributing heads are split over this many CTAs per tile
+  const __half* qk_lo;     // mma.sync kernel, optional: fp16 residues of the queries and keys ([T, 2d])
 };
 cudaError_t launch_contact_accumulate(const ContactParams& p, cudaStream_t s);
 
